@@ -1,0 +1,132 @@
+"""Parity metrics and golden-fixture loading shared by the tests.
+
+Tolerances (the bar every parity test states):
+  * norm outputs (RMSNorm, fused add + RMSNorm): at most 1 ulp of the storage
+    dtype for bf16 / fp16, at most 4 ulp for fp32, measured as the distance
+    between the two values on the dtype's ordered bit lattice. Residual
+    outputs (round(x + r)) must be bit-exact.
+  * RoPE outputs: the norm-stage bar (k ulp on each normalised value n that
+    enters the rotation) propagated through it, plus k ulp of the output:
+      |actual - expected| <= k * (ulp(n_i)|c_i| + ulp(n_j)|s_i| + ulp(y)),
+    k = 1 for bf16 / fp16 and 4 for fp32. Near-zero outputs come from
+    cancellation, so an ulp of the output alone is not a meaningful bar.
+  * KV-cache slots: bit-exact.
+"""
+from __future__ import annotations
+
+from pathlib import Path
+
+import numpy as np
+import torch
+
+GOLDEN = Path(__file__).resolve().parent / "golden"
+NAMES = {"fp32": torch.float32, "fp16": torch.float16, "bf16": torch.bfloat16}
+MANTISSA_BITS = {torch.float32: 23, torch.float16: 10, torch.bfloat16: 7}
+MIN_EXPONENT = {torch.float32: -126, torch.float16: -14, torch.bfloat16: -126}
+
+
+def ordered(t: torch.Tensor) -> torch.Tensor:
+    """Map floats to int64 so that adjacent representable values differ by 1."""
+    if t.dtype == torch.float32:
+        bits = t.contiguous().view(torch.int32).to(torch.int64)
+        mag = bits & 0x7FFFFFFF
+        return torch.where(bits < 0, -mag, mag)
+    bits = t.contiguous().view(torch.int16).to(torch.int64) & 0xFFFF
+    mag = bits & 0x7FFF
+    return torch.where(bits >= 0x8000, -mag, mag)
+
+
+def ulp_distance(a: torch.Tensor, b: torch.Tensor) -> torch.Tensor:
+    assert a.dtype == b.dtype and a.shape == b.shape, (a.dtype, b.dtype, a.shape, b.shape)
+    return (ordered(a.cpu()) - ordered(b.cpu())).abs()
+
+
+def ulp_at(magnitude: torch.Tensor, dtype: torch.dtype) -> torch.Tensor:
+    """Spacing of `dtype` values at |magnitude| (float64)."""
+    m = magnitude.abs().to(torch.float64)
+    exponent = torch.floor(torch.log2(torch.clamp(m, min=1e-300)))
+    exponent = torch.clamp(exponent, min=MIN_EXPONENT[dtype])
+    return torch.pow(2.0, exponent - MANTISSA_BITS[dtype])
+
+
+def default_norm_ulps(dtype: torch.dtype) -> int:
+    return 4 if dtype == torch.float32 else 1
+
+
+def assert_ulp_close(actual: torch.Tensor, expected: torch.Tensor, max_ulp: int | None = None,
+                     what: str = "") -> None:
+    max_ulp = default_norm_ulps(expected.dtype) if max_ulp is None else max_ulp
+    d = ulp_distance(actual, expected)
+    worst = int(d.max()) if d.numel() else 0
+    if worst > max_ulp:
+        idx = int(d.flatten().argmax())
+        raise AssertionError(
+            f"{what}: {int((d > max_ulp).sum())} of {d.numel()} elements differ by more than "
+            f"{max_ulp} ulp (worst {worst} ulp at flat index {idx}: "
+            f"{actual.flatten()[idx].item()} vs {expected.flatten()[idx].item()})")
+
+
+def assert_bitwise_equal(actual: torch.Tensor, expected: torch.Tensor, what: str = "") -> None:
+    a, e = actual.detach().cpu().contiguous(), expected.detach().cpu().contiguous()
+    assert a.dtype == e.dtype and a.shape == e.shape, (what, a.dtype, e.dtype, a.shape, e.shape)
+    view = torch.int32 if a.dtype == torch.float32 else torch.int16
+    if a.dtype in (torch.int32, torch.int64):
+        view = a.dtype
+    mism = (a.view(view) != e.view(view))
+    if bool(mism.any()):
+        idx = int(mism.flatten().nonzero()[0])
+        raise AssertionError(f"{what}: {int(mism.sum())} of {mism.numel()} elements differ "
+                             f"bitwise (first at flat index {idx})")
+
+
+def rope_bound(x: torch.Tensor, weight: torch.Tensor, positions: torch.Tensor,
+               cos_sin: torch.Tensor, expected: torch.Tensor, k: int | None = None,
+               eps: float = 1e-6) -> torch.Tensor:
+    """Per-element RoPE tolerance for a [T, H, D] head tensor (see module doc);
+    n is evaluated in fp64 from the inputs."""
+    dtype = expected.dtype
+    k = (4 if dtype == torch.float32 else 1) if k is None else k
+    xd = x.detach().cpu().to(torch.float64)
+    d = xd.shape[-1]
+    half = d // 2
+    inv = torch.rsqrt(xd.square().mean(-1, keepdim=True) + eps)
+    n = xd * inv * weight.detach().cpu().to(torch.float64)
+    rows = cos_sin.detach().cpu().reshape(-1, d).to(torch.float64)[positions.cpu().long()]
+    c, s = rows[:, None, :half].abs(), rows[:, None, half:].abs()
+    u1, u2 = ulp_at(n[..., :half], dtype), ulp_at(n[..., half:], dtype)
+    prop = torch.cat((u1 * c + u2 * s, u2 * c + u1 * s), dim=-1)
+    return k * (prop + ulp_at(expected.detach().cpu(), dtype))
+
+
+def assert_rope_close(actual: torch.Tensor, expected: torch.Tensor, bound: torch.Tensor,
+                      what: str = "") -> None:
+    a = actual.detach().cpu().to(torch.float64)
+    e = expected.detach().cpu().to(torch.float64)
+    err = (a - e).abs()
+    bad = err > bound
+    if bool(bad.any()):
+        idx = int(bad.flatten().nonzero()[0])
+        raise AssertionError(
+            f"{what}: {int(bad.sum())} of {bad.numel()} RoPE outputs exceed the propagated "
+            f"bound (first at flat index {idx}: {a.flatten()[idx].item()} vs "
+            f"{e.flatten()[idx].item()}, bound {bound.flatten()[idx].item()})")
+
+
+def load_golden(name: str) -> dict:
+    """Fixture `name` as a dict of CPU tensors (bf16 restored from raw bits)."""
+    with np.load(GOLDEN / f"{name}.npz") as data:
+        raw = {k: data[k] for k in data.files}
+    dtype = NAMES[str(raw.pop("dtype"))]
+    out = {"dtype": dtype}
+    for key, arr in raw.items():
+        if arr.dtype == np.uint16:
+            out[key] = torch.from_numpy(arr.view(np.int16).copy()).view(torch.bfloat16)
+        elif arr.ndim == 0:
+            out[key] = arr.item()
+        else:
+            out[key] = torch.from_numpy(arr.copy())
+    return out
+
+
+def golden_names(prefix: str) -> list[str]:
+    return sorted(p.stem for p in GOLDEN.glob(f"{prefix}*.npz"))
