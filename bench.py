@@ -1,0 +1,544 @@
+"""Benchmark: achieved HBM GB/s (% of B200 peak) and us/call of the fused
+normalisation path, at 1..8 GPUs.
+
+Workload (one "step"): the in-place residual-add + RMSNorm sweep the metric is
+quoted on -- tokens in {1, 4, 16, 64, 256, 1024} x hidden in {768, 1024, 2048,
+4096} x {bf16, fp16}, x and residual ~ N(0, 1), weight ~ N(1, 0.1), eps 1e-6:
+48 calls of ``fused_add_rms_norm_inplace``, replayed as one CUDA graph. L2 is
+flushed (a 512 MiB write) before every timed step, outside the timed events.
+``value`` = algorithmic bytes of all ranks' steps / max-over-ranks device time.
+
+Also reported on the same line:
+  * ``roofline`` -- the dominant kernel of the step (largest total time), its
+    algorithmic bytes per launch over its mean CUDA-event launch duration
+    (each launch after an L2 flush), against the measured HBM copy peak;
+  * ``e2e`` -- the same sweep through the public API with the inputs copied
+    from pinned host memory and both outputs copied back inside the timed
+    region;
+  * ``per_op`` -- us/call and GB/s of every operator at the other workload
+    shapes (batch-1 and wide-batch decode Q/K norm + RoPE + KV store, the
+    prefill fused add [65536, 8192] and Q/K prefill of 32768 tokens, and the
+    fp32 RMSNorm rows), each launch after an L2 flush;
+  * ``cpu_baseline`` -- the C oracle on the host cores (rank 0, N=1 only).
+
+``--impl reference`` times the reference path's CPU implementation (the C
+restatement of its PyTorch oracle) on the host cores instead.
+
+Multi-GPU: launched one process per GPU by torchrun; each rank runs the same
+per-rank workload on its own GPU (rows / sequences sharded, no collective on
+the data path). NCCL is used only for the barrier and the max-over-ranks time.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import math
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+from pathlib import Path
+
+import torch
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT / "sm120-norm-fusion-kernels_b200"))
+sys.path.insert(0, str(ROOT))
+
+TOKENS = (1, 4, 16, 64, 256, 1024)
+HIDDEN = (768, 1024, 2048, 4096)
+DTYPES = {"bf16": torch.bfloat16, "fp16": torch.float16}
+EPS = 1e-6
+FLUSH_BYTES = 512 * 1024 * 1024
+FALLBACK_HBM_GBS = 6650.0
+
+
+# ---------------------------------------------------------------------------
+# byte models (algorithmic bytes per call)
+# ---------------------------------------------------------------------------
+def fused_bytes(t: int, h: int, s: int) -> int:
+    return 4 * t * h * s + h * s  # read x, r; write x, r; weight once
+
+
+def rms_bytes(t: int, h: int, s: int) -> int:
+    return 2 * t * h * s + h * s
+
+
+def qk_kv_bytes(t: int, hq: int, hk: int, s: int, d: int = 128) -> int:
+    # q, k read + written; v read; k-cache and v-cache written; position (8 B),
+    # slot (4 B) and one fp32 cos/sin row (4 * d B) per token; two weights once.
+    return t * (s * d * (2 * hq + 5 * hk) + 8 + 4 + 4 * d) + 2 * d * s
+
+
+def sweep_shapes():
+    return [(t, h, name) for name in DTYPES for t in TOKENS for h in HIDDEN]
+
+
+# ---------------------------------------------------------------------------
+# environment
+# ---------------------------------------------------------------------------
+class Dist:
+    def __init__(self):
+        self.world = int(os.environ.get("WORLD_SIZE", "1"))
+        self.rank = int(os.environ.get("RANK", "0"))
+        self.local_rank = int(os.environ.get("LOCAL_RANK", "0"))
+        self.pg = None
+
+    def init(self):
+        if self.world > 1:
+            import datetime
+
+            import torch.distributed as dist
+            torch.cuda.set_device(self.local_rank)
+            dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                    device_id=torch.device("cuda", self.local_rank))
+            self.pg = dist
+        else:
+            torch.cuda.set_device(0)
+
+    def barrier(self):
+        torch.cuda.synchronize()
+        if self.pg is not None:
+            self.pg.barrier(device_ids=[self.local_rank])
+        torch.cuda.synchronize()
+
+    def max(self, value: float) -> float:
+        if self.pg is None:
+            return value
+        t = torch.tensor([value], dtype=torch.float64, device="cuda")
+        self.pg.all_reduce(t, op=self.pg.ReduceOp.MAX)
+        return float(t.item())
+
+    def close(self):
+        if self.pg is not None:
+            self.pg.destroy_process_group()
+
+
+def measured_hbm_peak():
+    path = ROOT / "MEASURED_PEAKS.json"
+    try:
+        data = json.loads(path.read_text())
+        return float(data["hbm_gbs"]), "measured (MEASURED_PEAKS.json hbm_gbs, copy burst)"
+    except Exception:
+        return FALLBACK_HBM_GBS, "fallback (6.65 TB/s pool figure; MEASURED_PEAKS.json absent)"
+
+
+def dram_traffic_per_launch():
+    """dram bytes read + written per launch of the dominant kernel, from the
+    committed ncu summary (profiles/dram_traffic.txt), or None."""
+    path = ROOT / "profiles" / "dram_traffic.txt"
+    if not path.exists():
+        return None
+    out = {}
+    for line in path.read_text().splitlines():
+        if "=" in line and not line.startswith("#"):
+            k, v = line.split("=", 1)
+            out[k.strip()] = v.strip()
+    return out
+
+
+class ClockSampler:
+    """nvidia-smi samples of SM clock and throttle reasons during the timed region."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpus: str | None):
+        self.gpus = gpus
+        self.proc = None
+        self.lines: list[str] = []
+
+    def __enter__(self):
+        cmd = ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+               "-lms", "100"]
+        if self.gpus:
+            cmd += ["-i", self.gpus]
+        try:
+            self.proc = subprocess.Popen(cmd, stdout=subprocess.PIPE, stderr=subprocess.DEVNULL,
+                                         text=True)
+            self.reader = threading.Thread(target=self._read, daemon=True)
+            self.reader.start()
+        except OSError:
+            self.proc = None
+        return self
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def __exit__(self, *exc):
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+            self.reader.join(timeout=2)
+
+    def summary(self):
+        rows = []
+        for line in self.lines:
+            parts = [p.strip() for p in line.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                rows.append((int(parts[0]), float(parts[1]), float(parts[2]), parts[5:9]))
+            except ValueError:
+                continue
+        if not rows:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"], "samples": 0}
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({names[i] for r in rows for i, flag in enumerate(r[3])
+                          if flag.lower() == "active"})
+        return {"sm_mhz": statistics.median(r[1] for r in rows),
+                "sm_max_mhz": max(r[2] for r in rows), "reasons": reasons,
+                "samples": len(rows)}
+
+
+# ---------------------------------------------------------------------------
+# GPU arm
+# ---------------------------------------------------------------------------
+class Flusher:
+    def __init__(self):
+        self.buf = torch.empty(FLUSH_BYTES, dtype=torch.uint8, device="cuda")
+
+    def __call__(self):
+        self.buf.fill_(1)
+
+
+def event_pair():
+    return torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+
+
+def time_launches(fn, flush: Flusher, reps: int) -> float:
+    """Mean device time (us) of `fn`, each launch preceded by an L2 flush."""
+    times = []
+    for _ in range(reps):
+        flush()
+        a, b = event_pair()
+        a.record()
+        fn()
+        b.record()
+        b.synchronize()
+        times.append(a.elapsed_time(b) * 1e3)
+    return statistics.fmean(times)
+
+
+class SweepData:
+    def __init__(self, seed: int):
+        g = torch.Generator(device="cuda").manual_seed(seed)
+        self.items = []
+        for t, h, name in sweep_shapes():
+            dt = DTYPES[name]
+            x = torch.randn(t, h, device="cuda", generator=g).to(dt)
+            r = torch.randn(t, h, device="cuda", generator=g).to(dt)
+            w = (1.0 + 0.1 * torch.randn(h, device="cuda", generator=g)).to(dt)
+            self.items.append((t, h, name, x, r, w))
+        self.bytes = sum(fused_bytes(t, h, x.element_size()) for t, h, _, x, _, _ in self.items)
+
+    def run(self, ops):
+        for _, _, _, x, r, w in self.items:
+            ops.fused_add_rms_norm_inplace(x, r, w, EPS)
+
+
+def gpu_arm(args, dist: Dist) -> dict:
+    import sm120_rmsnorm as ops
+
+    dev = torch.device("cuda", torch.cuda.current_device())
+    flush = Flusher()
+    data = SweepData(seed=1234 + dist.rank)
+
+    # CUDA graph of one step (48 launches)
+    for _ in range(3):
+        data.run(ops)
+    torch.cuda.synchronize()
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph):
+        data.run(ops)
+    launches_per_step = len(data.items)
+
+    for _ in range(args.warmup):
+        flush()
+        graph.replay()
+    dist.barrier()
+    starts, ends = [], []
+    gpus = os.environ.get("CUDA_VISIBLE_DEVICES") if dist.world == 1 else None
+    with ClockSampler(gpus if dist.rank == 0 else "none") as clocks:
+        dist.barrier()
+        for _ in range(args.steps):
+            flush()
+            a, b = event_pair()
+            a.record()
+            graph.replay()
+            b.record()
+            starts.append(a)
+            ends.append(b)
+        dist.barrier()
+    step_ms = sum(a.elapsed_time(b) for a, b in zip(starts, ends)) / args.steps
+    step_ms_max = dist.max(step_ms)
+    value = data.bytes * dist.world / (step_ms_max * 1e-3) / 1e9
+
+    # per-kernel launch durations (same shapes, each launch after a flush)
+    per_shape = []
+    for t, h, name, x, r, w in data.items:
+        us = time_launches(lambda: ops.fused_add_rms_norm_inplace(x, r, w, EPS), flush,
+                           max(3, args.reps))
+        per_shape.append({"tokens": t, "hidden": h, "dtype": name, "us": round(dist.max(us), 3),
+                          "bytes": fused_bytes(t, h, x.element_size())})
+    for p in per_shape:
+        p["gbs"] = round(p["bytes"] / (p["us"] * 1e-6) / 1e9, 1)
+    dominant = max(per_shape, key=lambda p: p["us"])
+    peak, peak_source = measured_hbm_peak()
+    traffic = dram_traffic_per_launch()
+    traffic_value = None
+    if traffic and traffic.get("config") == f"fused_add_rms_norm_inplace {dominant['dtype']} " \
+                                            f"{dominant['tokens']}x{dominant['hidden']}":
+        traffic_value = int(float(traffic.get("dram_bytes_per_launch", "nan")))
+    roofline = {"bound": "hbm", "achieved": dominant["gbs"], "peak": peak, "unit": "GB/s",
+                "frac": round(dominant["gbs"] / peak, 4), "traffic": traffic_value,
+                "kernel": f"fused_add_rms_norm_inplace {dominant['dtype']} "
+                          f"{dominant['tokens']}x{dominant['hidden']}",
+                "algorithmic_bytes_per_launch": dominant["bytes"],
+                "launch_us": dominant["us"], "peak_source": peak_source + ", of measured"
+                if peak_source.startswith("measured") else peak_source + ", of fallback"}
+
+    # end to end through the public API with pinned host buffers
+    host = [(x.cpu().pin_memory(), r.cpu().pin_memory()) for _, _, _, x, r, _ in data.items]
+    outs = [(torch.empty_like(hx).pin_memory(), torch.empty_like(hr).pin_memory())
+            for hx, hr in host]
+    h2d = sum(2 * hx.numel() * hx.element_size() for hx, _ in host)
+
+    def e2e_step():
+        for (t, h, name, x, r, w), (hx, hr), (ox, orr) in zip(data.items, host, outs):
+            x.copy_(hx, non_blocking=True)
+            r.copy_(hr, non_blocking=True)
+            ops.fused_add_rms_norm_inplace(x, r, w, EPS)
+            ox.copy_(x, non_blocking=True)
+            orr.copy_(r, non_blocking=True)
+
+    for _ in range(args.warmup):
+        e2e_step()
+    dist.barrier()
+    a, b = event_pair()
+    a.record()
+    e2e_steps = max(3, args.steps // 5)
+    for _ in range(e2e_steps):
+        e2e_step()
+    b.record()
+    b.synchronize()
+    e2e_ms = dist.max(a.elapsed_time(b) / e2e_steps)
+    e2e = {"value": round(data.bytes * dist.world / (e2e_ms * 1e-3) / 1e9, 2), "unit": "GB/s",
+           "ms_per_step": round(e2e_ms, 4), "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": h2d,
+           "path": "sm120_rmsnorm.fused_add_rms_norm_inplace with pinned-host copies"}
+
+    per_op = {} if args.skip_per_op else per_op_suite(ops, flush, dist, args)
+    clock = clocks.summary() if dist.rank == 0 else None
+
+    return {
+        "metric": "achieved HBM GB/s (% of B200 peak) and us/call per op at 1/2/4/8 GPUs",
+        "value": round(value, 2), "unit": "GB/s", "n_gpus": dist.world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": round(step_ms_max, 5), "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "bf16+fp16 (fp32 accumulate)",
+        "data": "synthetic (seeded N(0,1) activations, N(1,0.1) weights)",
+        "config": {"workload": "in-place residual add + RMSNorm sweep: tokens "
+                               "{1,4,16,64,256,1024} x hidden {768,1024,2048,4096} x "
+                               "{bf16,fp16}, one CUDA graph of 48 launches per step",
+                   "global_batch": len(data.items) * dist.world,
+                   "bytes_per_step_per_gpu": data.bytes, "parallelism": f"dp{dist.world}"
+                   f" (each rank its own rows, no collective)",
+                   "l2": "flushed (512 MiB write) before every timed step and every "
+                         "per-launch timing, outside the events"},
+        "roofline": roofline, "e2e": e2e, "gpu_launches": launches_per_step * args.steps,
+        "clocks": clock, "per_shape": per_shape, "per_op": per_op,
+        "device": torch.cuda.get_device_name(dev),
+    }
+
+
+def per_op_suite(ops, flush: Flusher, dist: Dist, args) -> dict:
+    """us/call and GB/s of each operator at the other workload shapes."""
+    out = {}
+    reps = max(3, args.reps)
+    g = torch.Generator(device="cuda").manual_seed(99 + dist.rank)
+    bf = torch.bfloat16
+
+    def rope_cache(n):
+        inv = 1.0 / (1e6 ** (torch.arange(0, 128, 2, dtype=torch.float32, device="cuda") / 128))
+        f = torch.outer(torch.arange(n, dtype=torch.float32, device="cuda"), inv)
+        return torch.cat((f.cos(), f.sin()), dim=-1)
+
+    cache = rope_cache(32768)
+
+    def record(name, us, nbytes):
+        us = dist.max(us)
+        out[name] = {"us": round(us, 3), "bytes": nbytes,
+                     "gbs": round(nbytes / (us * 1e-6) / 1e9, 1)}
+
+    # fp32 RMSNorm rows of 1024 (the CPU-runnable workload), on the GPU
+    for t in (1, 4, 16, 64, 256):
+        x = torch.randn(t, 1024, device="cuda", generator=g)
+        w = 1.0 + 0.1 * torch.randn(1024, device="cuda", generator=g)
+        y = torch.empty_like(x)
+        record(f"rms_norm fp32 {t}x1024",
+               time_launches(lambda: ops.rms_norm_out(x, w, y, EPS), flush, reps),
+               rms_bytes(t, 1024, 4))
+
+    # Qwen3 decode QK norm + RoPE + paged KV store
+    def qk_case(name, b, hq, hk, blocks, positions, slots):
+        q = torch.randn(b, hq, 128, device="cuda", generator=g).to(bf)
+        k = torch.randn(b, hk, 128, device="cuda", generator=g).to(bf)
+        v = torch.randn(b, hk, 128, device="cuda", generator=g).to(bf)
+        qw = (1 + 0.1 * torch.randn(128, device="cuda", generator=g)).to(bf)
+        kw = (1 + 0.1 * torch.randn(128, device="cuda", generator=g)).to(bf)
+        kc = torch.zeros(blocks, 16, hk, 128, device="cuda", dtype=bf)
+        vc = torch.zeros_like(kc)
+        fn = lambda: ops.fused_qk_rms_norm_rope_kv(q, k, v, qw, kw, positions, cache, kc, vc,
+                                                   slots, EPS)
+        record(name, time_launches(fn, flush, reps), qk_kv_bytes(b, hq, hk, 2))
+        del q, k, v, kc, vc
+
+    cpu_g = torch.Generator().manual_seed(7 + dist.rank)
+    qk_case("qk_kv decode bf16 B=1 16/8", 1, 16, 8, 2048,
+            torch.randint(0, 32768, (1,), generator=cpu_g).cuda(),
+            torch.randint(0, 2048 * 16, (1,), generator=cpu_g).to(torch.int32).cuda())
+    for b in (64, 256, 1024):
+        qk_case(f"qk_kv decode bf16 B={b} 32/8", b, 32, 8, 65536,
+                torch.randperm(32768, generator=cpu_g)[:b].cuda(),
+                torch.randperm(65536 * 16, generator=cpu_g)[:b].to(torch.int32).cuda())
+    qk_case("qk_kv prefill bf16 32768 tokens 64/8", 32768, 64, 8, 2048,
+            torch.arange(32768, device="cuda"),
+            torch.arange(32768, device="cuda", dtype=torch.int32))
+
+    # prefill residual add + RMSNorm
+    x = torch.randn(65536, 8192, device="cuda", generator=g).to(bf)
+    r = torch.randn(65536, 8192, device="cuda", generator=g).to(bf)
+    w = (1 + 0.1 * torch.randn(8192, device="cuda", generator=g)).to(bf)
+    record("fused_add_rms_norm_inplace prefill bf16 65536x8192",
+           time_launches(lambda: ops.fused_add_rms_norm_inplace(x, r, w, EPS), flush, reps),
+           fused_bytes(65536, 8192, 2))
+    del x, r
+    return out
+
+
+# ---------------------------------------------------------------------------
+# CPU arms (the oracle is the checker and the CPU baseline, nothing else)
+# ---------------------------------------------------------------------------
+def host_threads() -> int:
+    try:
+        return len(os.sched_getaffinity(0))
+    except AttributeError:
+        return os.cpu_count() or 1
+
+
+def cpu_sweep_gbs(seconds: float, threads: int, passes: int | None = None):
+    from oracle import oracle
+
+    oracle.build()
+    oracle.set_threads(threads)
+    g = torch.Generator().manual_seed(4321)
+    items = []
+    for t, h, name in sweep_shapes():
+        dt = DTYPES[name]
+        x = torch.randn(t, h, generator=g).to(dt)
+        r = torch.randn(t, h, generator=g).to(dt)
+        w = (1 + 0.1 * torch.randn(h, generator=g)).to(dt)
+        items.append((x, r, w))
+    total = sum(fused_bytes(x.shape[0], x.shape[1], x.element_size()) for x, _, _ in items)
+    for x, r, w in items:  # warm-up pass
+        oracle.fused_add_rms_norm_out(x, r, w, x, r, EPS)
+    done, t0 = 0, time.perf_counter()
+    while True:
+        for x, r, w in items:
+            oracle.fused_add_rms_norm_out(x, r, w, x, r, EPS)
+        done += 1
+        elapsed = time.perf_counter() - t0
+        if (passes is not None and done >= passes) or (passes is None and elapsed >= seconds):
+            break
+    return total * done / elapsed / 1e9, done, elapsed
+
+
+def reference_arm(args, dist: Dist) -> dict:
+    """The reference path's CPU implementation (C restatement of its PyTorch
+    oracle) on the host cores, on the same sweep; rank 0 only."""
+    threads = host_threads()
+    from oracle import oracle
+
+    oracle.build()
+    oracle.set_threads(threads)
+    for _ in range(args.warmup):
+        cpu_sweep_gbs(0, threads, passes=1)
+    gbs, passes, elapsed = cpu_sweep_gbs(0, threads, passes=args.steps)
+    sample = (f"{passes} passes over the 48-call sweep (one step each), "
+              f"{elapsed:.2f} s of CPU time")
+    return {
+        "impl": "reference",
+        "metric": "achieved HBM GB/s (% of B200 peak) and us/call per op at 1/2/4/8 GPUs",
+        "value": round(gbs, 3), "unit": "GB/s", "n_gpus": dist.world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": round(elapsed / passes * 1e3, 3),
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+        "dtype": "bf16+fp16 (fp32 accumulate)", "data": "synthetic",
+        "config": {"workload": "in-place residual add + RMSNorm sweep: tokens "
+                               "{1,4,16,64,256,1024} x hidden {768,1024,2048,4096} x "
+                               "{bf16,fp16}", "parallelism": "host cores"},
+        "cpu_baseline": {"value": round(gbs, 3), "unit": "GB/s", "cores": threads,
+                         "kind": "port", "sample": sample},
+        "e2e": {"value": round(gbs, 3), "unit": "GB/s", "h2d_bytes_per_step": 0,
+                "d2h_bytes_per_step": 0},
+        "note": "the reference's CPU path is its PyTorch oracle (sm120_rmsnorm/reference.py), "
+                "which cannot travel; this is its C restatement (oracle/norm_oracle.c), "
+                "pinned to the reference's own outputs by the golden-vector tests",
+    }
+
+
+# ---------------------------------------------------------------------------
+def main():
+    parser = argparse.ArgumentParser(description=__doc__.splitlines()[0])
+    parser.add_argument("--gpus", type=int, default=1)
+    parser.add_argument("--steps", type=int, default=50)
+    parser.add_argument("--warmup", type=int, default=5)
+    parser.add_argument("--reps", type=int, default=10, help="launches per per-kernel timing")
+    parser.add_argument("--impl", choices=["b200", "reference"], default="b200")
+    parser.add_argument("--cpu-seconds", type=float, default=10.0)
+    parser.add_argument("--skip-per-op", action="store_true")
+    parser.add_argument("--skip-cpu", action="store_true")
+    args = parser.parse_args()
+    if args.warmup < 3:
+        parser.error("--warmup must be at least 3")
+
+    dist = Dist()
+    if args.gpus > 1 and dist.world == 1:
+        # not under torchrun: relaunch one process per GPU
+        cmd = [sys.executable, "-m", "torch.distributed.run", "--nnodes=1",
+               f"--nproc-per-node={args.gpus}", "--master-addr=127.0.0.1",
+               "--master-port=29517", *sys.argv]
+        raise SystemExit(subprocess.call(cmd))
+    if dist.world > 1 and args.gpus != dist.world:
+        print(f"warning: --gpus {args.gpus} but WORLD_SIZE {dist.world}; using WORLD_SIZE",
+              file=sys.stderr)
+
+    if args.impl == "reference":
+        if dist.rank != 0:
+            return
+        print(json.dumps(reference_arm(args, dist)))
+        return
+
+    dist.init()
+    try:
+        line = gpu_arm(args, dist)
+        if dist.rank == 0 and dist.world == 1 and not args.skip_cpu:
+            threads = host_threads()
+            gbs, passes, elapsed = cpu_sweep_gbs(args.cpu_seconds, threads)
+            line["cpu_baseline"] = {
+                "value": round(gbs, 3), "unit": "GB/s", "cores": threads, "kind": "port",
+                "sample": f"{passes} passes over the 48-call sweep in {elapsed:.1f} s "
+                          f"(C restatement of the reference's PyTorch oracle, OpenMP)"}
+        if dist.rank == 0:
+            print(json.dumps(line))
+    finally:
+        dist.close()
+
+
+if __name__ == "__main__":
+    main()

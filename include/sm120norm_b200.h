@@ -34,6 +34,12 @@ extern "C" {
 
 #define SM120N_ABI_VERSION 1
 
+#if defined(__GNUC__)
+#define SM120N_API __attribute__((visibility("default")))
+#else
+#define SM120N_API
+#endif
+
 /* Element type of activations, weights, outputs and KV caches. */
 typedef enum sm120n_dtype {
   SM120N_F32 = 0,
@@ -49,13 +55,13 @@ typedef enum sm120n_status {
 } sm120n_status;
 
 /* Version of this ABI (SM120N_ABI_VERSION of the built library). */
-int sm120n_abi_version(void);
+SM120N_API int sm120n_abi_version(void);
 
 /* Message describing the last failing call made by this thread ("" if none). */
-const char* sm120n_last_error(void);
+SM120N_API const char* sm120n_last_error(void);
 
 /* Static name of a status code. */
-const char* sm120n_status_string(int status);
+SM120N_API const char* sm120n_status_string(int status);
 
 /*
  * Programmatic dependent launch: when enabled (the default), kernels are
@@ -64,8 +70,8 @@ const char* sm120n_status_string(int status);
  * waits for the preceding grid to complete before touching global memory, so
  * results do not depend on this switch. Process-wide.
  */
-void sm120n_set_programmatic_launch(int enabled);
-int sm120n_get_programmatic_launch(void);
+SM120N_API void sm120n_set_programmatic_launch(int enabled);
+SM120N_API int sm120n_get_programmatic_launch(void);
 
 /*
  * Number of bounded waits that expired in kernels on the current device since
@@ -73,8 +79,8 @@ int sm120n_get_programmatic_launch(void);
  * means a pipelined kernel gave up waiting on its own asynchronous copies and
  * skipped the affected rows. Synchronises the current device.
  */
-int sm120n_get_device_faults(uint32_t* out_count);
-int sm120n_reset_device_faults(void);
+SM120N_API int sm120n_get_device_faults(uint32_t* out_count);
+SM120N_API int sm120n_reset_device_faults(void);
 
 /*
  * RMSNorm: output[i, :] = round(x[i, :] * (1 / sqrt(mean(x[i, :]^2) + eps)) * weight)
@@ -82,7 +88,7 @@ int sm120n_reset_device_faults(void);
  * Replaces rms_norm_out_cuda, csrc/rmsnorm_kernels.cu:482-524 (and
  * rms_norm_cuda :472-480, whose allocation stays with the caller).
  */
-int sm120n_rms_norm(const void* input, const void* weight, void* output,
+SM120N_API int sm120n_rms_norm(const void* input, const void* weight, void* output,
                     int64_t rows, int64_t hidden_size, int dtype,
                     float epsilon, int version, void* stream);
 
@@ -97,7 +103,7 @@ int sm120n_rms_norm(const void* input, const void* weight, void* output,
  * fused_add_rms_norm_inplace_cuda :526-537 and fused_add_rms_norm_cuda
  * :711-722.
  */
-int sm120n_fused_add_rms_norm(const void* input, const void* residual,
+SM120N_API int sm120n_fused_add_rms_norm(const void* input, const void* residual,
                               const void* weight, void* output,
                               void* residual_output, int64_t rows,
                               int64_t hidden_size, int dtype, float epsilon,
@@ -114,7 +120,7 @@ int sm120n_fused_add_rms_norm(const void* input, const void* residual,
  * [0, rope_positions) is left unchanged.
  * Replaces fused_qk_rms_norm_rope_cuda, csrc/rmsnorm_kernels.cu:539-609.
  */
-int sm120n_fused_qk_rms_norm_rope(void* query, void* key,
+SM120N_API int sm120n_fused_qk_rms_norm_rope(void* query, void* key,
                                   const void* query_weight,
                                   const void* key_weight,
                                   const int64_t* positions,
@@ -133,7 +139,7 @@ int sm120n_fused_qk_rms_norm_rope(void* query, void* key,
  * version 1 or 4 (warps per thread block).
  * Replaces fused_qk_rms_norm_rope_kv_cuda, csrc/rmsnorm_kernels.cu:611-709.
  */
-int sm120n_fused_qk_rms_norm_rope_kv(
+SM120N_API int sm120n_fused_qk_rms_norm_rope_kv(
     void* query, void* key, const void* value, const void* query_weight,
     const void* key_weight, const int64_t* positions,
     const float* cos_sin_cache, void* key_cache, void* value_cache,

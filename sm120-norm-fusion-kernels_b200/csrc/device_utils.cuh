@@ -1,0 +1,165 @@
+// device_utils.cuh -- element packs, rounding and reductions shared by the
+// B200 normalisation kernels.
+//
+// Numerics contract (matches the reference's PyTorch oracle on CPU, op by op):
+//   * every fp32 product, sum and difference is rounded on its own: the
+//     kernels use __fmul_rn / __fadd_rn / __fsub_rn, which the compiler never
+//     contracts into an FMA;
+//   * inv_rms = 1 / sqrt(sum_sq / n + eps) with correctly rounded divide and
+//     square root (__fdiv_rn, __fsqrt_rn), which is how PyTorch's CPU rsqrt
+//     and mean evaluate;
+//   * fp32 -> bf16 / fp16 conversions round to nearest even.
+// The only freedom left is the order of the fp32 sum of squares.
+#pragma once
+
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+namespace sm120n {
+
+constexpr int kWarpSize = 32;
+constexpr unsigned kFullMask = 0xffffffffu;
+
+// ---------------------------------------------------------------------------
+// 16-byte packs. A pack holds kElems elements of T in a uint4; element e sits
+// in word e / (4 / sizeof(T)), low half first (little endian).
+// ---------------------------------------------------------------------------
+template <typename T>
+struct Pack;
+
+template <>
+struct Pack<float> {
+  static constexpr int kElems = 4;
+  __device__ __forceinline__ static void to_f32(const uint4& p, float* f) {
+    f[0] = __uint_as_float(p.x);
+    f[1] = __uint_as_float(p.y);
+    f[2] = __uint_as_float(p.z);
+    f[3] = __uint_as_float(p.w);
+  }
+  __device__ __forceinline__ static uint4 from_f32(const float* f) {
+    return make_uint4(__float_as_uint(f[0]), __float_as_uint(f[1]),
+                      __float_as_uint(f[2]), __float_as_uint(f[3]));
+  }
+};
+
+template <>
+struct Pack<__nv_bfloat16> {
+  static constexpr int kElems = 8;
+  // bf16 -> fp32 is a 16-bit shift: exact.
+  __device__ __forceinline__ static void word_to_f32(uint32_t w, float& lo, float& hi) {
+    lo = __uint_as_float(w << 16);
+    hi = __uint_as_float(w & 0xffff0000u);
+  }
+  __device__ __forceinline__ static uint32_t f32_to_word(float lo, float hi) {
+    __nv_bfloat162 v = __floats2bfloat162_rn(lo, hi);  // .x = lo, .y = hi
+    return *reinterpret_cast<uint32_t*>(&v);
+  }
+  __device__ __forceinline__ static void to_f32(const uint4& p, float* f) {
+    word_to_f32(p.x, f[0], f[1]);
+    word_to_f32(p.y, f[2], f[3]);
+    word_to_f32(p.z, f[4], f[5]);
+    word_to_f32(p.w, f[6], f[7]);
+  }
+  __device__ __forceinline__ static uint4 from_f32(const float* f) {
+    return make_uint4(f32_to_word(f[0], f[1]), f32_to_word(f[2], f[3]),
+                      f32_to_word(f[4], f[5]), f32_to_word(f[6], f[7]));
+  }
+};
+
+template <>
+struct Pack<__half> {
+  static constexpr int kElems = 8;
+  __device__ __forceinline__ static void word_to_f32(uint32_t w, float& lo, float& hi) {
+    __half2 h = *reinterpret_cast<__half2*>(&w);
+    float2 f = __half22float2(h);
+    lo = f.x;
+    hi = f.y;
+  }
+  __device__ __forceinline__ static uint32_t f32_to_word(float lo, float hi) {
+    __half2 h = __floats2half2_rn(lo, hi);
+    return *reinterpret_cast<uint32_t*>(&h);
+  }
+  __device__ __forceinline__ static void to_f32(const uint4& p, float* f) {
+    word_to_f32(p.x, f[0], f[1]);
+    word_to_f32(p.y, f[2], f[3]);
+    word_to_f32(p.z, f[4], f[5]);
+    word_to_f32(p.w, f[6], f[7]);
+  }
+  __device__ __forceinline__ static uint4 from_f32(const float* f) {
+    return make_uint4(f32_to_word(f[0], f[1]), f32_to_word(f[2], f[3]),
+                      f32_to_word(f[4], f[5]), f32_to_word(f[6], f[7]));
+  }
+};
+
+// Scalar element access for the unaligned fallback kernels.
+template <typename T>
+struct Scalar;
+template <>
+struct Scalar<float> {
+  __device__ __forceinline__ static float load(const float* p) { return *p; }
+  __device__ __forceinline__ static void store(float* p, float v) { *p = v; }
+  __device__ __forceinline__ static float round(float v) { return v; }
+};
+template <>
+struct Scalar<__nv_bfloat16> {
+  __device__ __forceinline__ static float load(const __nv_bfloat16* p) { return __bfloat162float(*p); }
+  __device__ __forceinline__ static void store(__nv_bfloat16* p, float v) { *p = __float2bfloat16_rn(v); }
+  __device__ __forceinline__ static float round(float v) { return __bfloat162float(__float2bfloat16_rn(v)); }
+};
+template <>
+struct Scalar<__half> {
+  __device__ __forceinline__ static float load(const __half* p) { return __half2float(*p); }
+  __device__ __forceinline__ static void store(__half* p, float v) { *p = __float2half_rn(v); }
+  __device__ __forceinline__ static float round(float v) { return __half2float(__float2half_rn(v)); }
+};
+
+// ---------------------------------------------------------------------------
+// Global memory access, 16 bytes per thread per instruction.
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ uint4 load16(const void* p) {
+  return *reinterpret_cast<const uint4*>(p);
+}
+__device__ __forceinline__ void store16(void* p, const uint4& v) {
+  *reinterpret_cast<uint4*>(p) = v;
+}
+
+// ---------------------------------------------------------------------------
+// Reductions. The butterfly leaves the identical total in every lane of the
+// group (fp32 addition is commutative, so both partners compute the same sum).
+// ---------------------------------------------------------------------------
+template <int kLanes>
+__device__ __forceinline__ float group_allreduce_sum(float v) {
+#pragma unroll
+  for (int offset = kLanes / 2; offset > 0; offset >>= 1) {
+    v = __fadd_rn(v, __shfl_xor_sync(kFullMask, v, offset));
+  }
+  return v;
+}
+
+__device__ __forceinline__ float accumulate_squares(float acc, const float* f, int n) {
+#pragma unroll
+  for (int i = 0; i < n; ++i) acc = __fadd_rn(acc, __fmul_rn(f[i], f[i]));
+  return acc;
+}
+
+// 1 / sqrt(sum_sq / n + eps), every step correctly rounded.
+__device__ __forceinline__ float inverse_rms(float sum_sq, float n, float eps) {
+  return __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(sum_sq, n), eps)));
+}
+
+// ---------------------------------------------------------------------------
+// Programmatic dependent launch (sm_90+). griddepcontrol.wait returns once
+// every grid this one depends on has completed and its memory is visible; it
+// is a no-op when the kernel was launched without the PDL attribute. Every
+// kernel calls it before its first global-memory access.
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ void wait_for_upstream_grid() {
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+}
+__device__ __forceinline__ void release_downstream_grid() {
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+
+}  // namespace sm120n

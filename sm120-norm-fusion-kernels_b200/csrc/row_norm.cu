@@ -1,0 +1,481 @@
+// row_norm.cu -- RMSNorm and residual-add + RMSNorm over [rows, hidden] for
+// B200 (sm_100a), and their C-ABI entry points.
+//
+// Reference behaviour (paths in the reference project):
+//   sm120_rmsnorm/reference.py:5-24         the math and its rounding order
+//   csrc/rmsnorm_kernels.cu:472-524         rms_norm(_out)_cuda
+//   csrc/rmsnorm_kernels.cu:526-537, 711-801 fused_add_rms_norm{,_out,_inplace}_cuda
+//
+// The path is HBM-bound (about 10 flops per element), so every kernel here is
+// shaped around moving bytes: 16-byte loads and stores, each element read once
+// and written once, the row held in registers across the reduction, weights
+// loaded once per thread block, and persistent grids sized from the SM count
+// and the measured occupancy. Kernel families:
+//
+//   warp   one warp per row, rows <= 32 * 8 packs (<= 4 KiB of bf16);
+//          shuffle-only reduction, no block barrier.
+//   cta    one thread block per row, rows <= 1024 packs (16 KiB of bf16);
+//          one barrier per row (double-buffered partial sums).
+//   wide   one thread block per row, any 16-byte-aligned row; two passes
+//          (the second re-reads the row, which is then L2-resident).
+//   scalar any row, any alignment; element at a time, two passes.
+//
+// In-place use (output == input, residual_output == residual) is safe in all
+// families: each element is read before it is written and only by the thread
+// that writes it, and no pointer is declared __restrict__.
+#include <algorithm>
+
+#include "device_utils.cuh"
+#include "runtime.h"
+
+namespace sm120n {
+
+// Bounded waits that expired in the pipelined kernels of this file since the
+// last reset (see sm120n_get_device_faults). Zero in correct operation.
+__device__ unsigned int g_expired_waits = 0;
+
+namespace {
+
+template <typename T>
+struct RowArgs {
+  const T* input;
+  const T* residual;  // nullptr for plain RMSNorm
+  const T* weight;
+  T* output;
+  T* residual_output;  // nullptr for plain RMSNorm
+  int64_t rows;
+  int hidden;
+  float epsilon;
+};
+
+// s = round(x + r) for one pack (kAdd), returned packed; f receives fp32 s.
+template <typename T, bool kAdd>
+__device__ __forceinline__ uint4 combine(const uint4& x, const uint4& r, float* f) {
+  using P = Pack<T>;
+  P::to_f32(x, f);
+  if constexpr (kAdd) {
+    float g[P::kElems];
+    P::to_f32(r, g);
+#pragma unroll
+    for (int e = 0; e < P::kElems; ++e) f[e] = __fadd_rn(f[e], g[e]);
+    const uint4 s = P::from_f32(f);
+    P::to_f32(s, f);  // the rounded sum is what the oracle squares
+    return s;
+  } else {
+    return x;
+  }
+}
+
+// round(round32(s * inv) * w) for one pack.
+template <typename T>
+__device__ __forceinline__ uint4 scale(const uint4& s, const uint4& w, float inv) {
+  using P = Pack<T>;
+  float f[P::kElems], g[P::kElems];
+  P::to_f32(s, f);
+  P::to_f32(w, g);
+#pragma unroll
+  for (int e = 0; e < P::kElems; ++e) f[e] = __fmul_rn(__fmul_rn(f[e], inv), g[e]);
+  return P::from_f32(f);
+}
+
+// ---- warp family -----------------------------------------------------------
+template <typename T, bool kAdd, int kPacksPerLane>
+__global__ void __launch_bounds__(256) row_norm_warp_kernel(RowArgs<T> a) {
+  constexpr int E = Pack<T>::kElems;
+  wait_for_upstream_grid();
+  release_downstream_grid();
+  const int lane = threadIdx.x & (kWarpSize - 1);
+  const int warps = blockDim.x / kWarpSize;
+  const int packs = a.hidden / E;
+  const float n = static_cast<float>(a.hidden);
+
+  uint4 w[kPacksPerLane];
+#pragma unroll
+  for (int i = 0; i < kPacksPerLane; ++i) {
+    const int c = lane + i * kWarpSize;
+    if (c < packs) w[i] = load16(a.weight + static_cast<int64_t>(c) * E);
+  }
+
+  for (int64_t row = static_cast<int64_t>(blockIdx.x) * warps + threadIdx.x / kWarpSize;
+       row < a.rows; row += static_cast<int64_t>(gridDim.x) * warps) {
+    const int64_t base = row * a.hidden;
+    uint4 s[kPacksPerLane], r[kPacksPerLane];
+#pragma unroll
+    for (int i = 0; i < kPacksPerLane; ++i) {
+      const int c = lane + i * kWarpSize;
+      if (c < packs) {
+        s[i] = load16(a.input + base + static_cast<int64_t>(c) * E);
+        if constexpr (kAdd) r[i] = load16(a.residual + base + static_cast<int64_t>(c) * E);
+      }
+    }
+    float sum_sq = 0.0f;
+#pragma unroll
+    for (int i = 0; i < kPacksPerLane; ++i) {
+      const int c = lane + i * kWarpSize;
+      if (c < packs) {
+        float f[E];
+        s[i] = combine<T, kAdd>(s[i], r[i], f);
+        sum_sq = accumulate_squares(sum_sq, f, E);
+      }
+    }
+    sum_sq = group_allreduce_sum<kWarpSize>(sum_sq);
+    const float inv = inverse_rms(sum_sq, n, a.epsilon);
+#pragma unroll
+    for (int i = 0; i < kPacksPerLane; ++i) {
+      const int c = lane + i * kWarpSize;
+      if (c < packs) {
+        const int64_t off = base + static_cast<int64_t>(c) * E;
+        if constexpr (kAdd) store16(a.residual_output + off, s[i]);
+        store16(a.output + off, scale<T>(s[i], w[i], inv));
+      }
+    }
+  }
+}
+
+// Block-wide sum with one barrier; `partial` is double buffered by `parity`
+// so the next row's writes cannot race this row's reads.
+__device__ __forceinline__ float block_allreduce_sum(float v, float (*partial)[kWarpSize],
+                                                     int parity) {
+  const int lane = threadIdx.x & (kWarpSize - 1);
+  const int warp = threadIdx.x / kWarpSize;
+  const int warps = blockDim.x / kWarpSize;
+  v = group_allreduce_sum<kWarpSize>(v);
+  if (lane == 0) partial[parity][warp] = v;
+  __syncthreads();
+  float total = 0.0f;
+  for (int i = 0; i < warps; ++i) total = __fadd_rn(total, partial[parity][i]);
+  return total;
+}
+
+// ---- cta family --------------------------------------------------------------
+template <typename T, bool kAdd, int kPacksPerThread, int kMaxThreads>
+__global__ void __launch_bounds__(kMaxThreads) row_norm_cta_kernel(RowArgs<T> a) {
+  constexpr int E = Pack<T>::kElems;
+  __shared__ float partial[2][kWarpSize];
+  wait_for_upstream_grid();
+  release_downstream_grid();
+  const int packs = a.hidden / E;
+  const float n = static_cast<float>(a.hidden);
+
+  uint4 w[kPacksPerThread];
+#pragma unroll
+  for (int i = 0; i < kPacksPerThread; ++i) {
+    const int c = threadIdx.x + i * blockDim.x;
+    if (c < packs) w[i] = load16(a.weight + static_cast<int64_t>(c) * E);
+  }
+
+  int parity = 0;
+  for (int64_t row = blockIdx.x; row < a.rows; row += gridDim.x) {
+    const int64_t base = row * a.hidden;
+    uint4 s[kPacksPerThread], r[kPacksPerThread];
+#pragma unroll
+    for (int i = 0; i < kPacksPerThread; ++i) {
+      const int c = threadIdx.x + i * blockDim.x;
+      if (c < packs) {
+        s[i] = load16(a.input + base + static_cast<int64_t>(c) * E);
+        if constexpr (kAdd) r[i] = load16(a.residual + base + static_cast<int64_t>(c) * E);
+      }
+    }
+    float sum_sq = 0.0f;
+#pragma unroll
+    for (int i = 0; i < kPacksPerThread; ++i) {
+      const int c = threadIdx.x + i * blockDim.x;
+      if (c < packs) {
+        float f[E];
+        s[i] = combine<T, kAdd>(s[i], r[i], f);
+        sum_sq = accumulate_squares(sum_sq, f, E);
+      }
+    }
+    const float inv = inverse_rms(block_allreduce_sum(sum_sq, partial, parity), n, a.epsilon);
+    parity ^= 1;
+#pragma unroll
+    for (int i = 0; i < kPacksPerThread; ++i) {
+      const int c = threadIdx.x + i * blockDim.x;
+      if (c < packs) {
+        const int64_t off = base + static_cast<int64_t>(c) * E;
+        if constexpr (kAdd) store16(a.residual_output + off, s[i]);
+        store16(a.output + off, scale<T>(s[i], w[i], inv));
+      }
+    }
+  }
+}
+
+// ---- wide family: any 16-byte-aligned row, two passes ------------------------
+template <typename T, bool kAdd>
+__global__ void __launch_bounds__(1024) row_norm_wide_kernel(RowArgs<T> a) {
+  constexpr int E = Pack<T>::kElems;
+  __shared__ float partial[2][kWarpSize];
+  wait_for_upstream_grid();
+  release_downstream_grid();
+  const int packs = a.hidden / E;
+  const float n = static_cast<float>(a.hidden);
+  int parity = 0;
+  for (int64_t row = blockIdx.x; row < a.rows; row += gridDim.x) {
+    const int64_t base = row * a.hidden;
+    float sum_sq = 0.0f;
+    for (int c = threadIdx.x; c < packs; c += blockDim.x) {
+      const int64_t off = base + static_cast<int64_t>(c) * E;
+      uint4 r;
+      if constexpr (kAdd) r = load16(a.residual + off);
+      float f[E];
+      const uint4 s = combine<T, kAdd>(load16(a.input + off), r, f);
+      if constexpr (kAdd) store16(a.residual_output + off, s);
+      sum_sq = accumulate_squares(sum_sq, f, E);
+    }
+    const float inv = inverse_rms(block_allreduce_sum(sum_sq, partial, parity), n, a.epsilon);
+    parity ^= 1;
+    // Pass 2 re-reads exactly the packs this thread handled in pass 1.
+    const T* source = kAdd ? a.residual_output : a.input;
+    for (int c = threadIdx.x; c < packs; c += blockDim.x) {
+      const int64_t off = base + static_cast<int64_t>(c) * E;
+      const uint4 s = load16(source + off);
+      store16(a.output + off, scale<T>(s, load16(a.weight + static_cast<int64_t>(c) * E), inv));
+    }
+  }
+}
+
+// ---- scalar family: any row, any alignment -----------------------------------
+template <typename T, bool kAdd>
+__global__ void __launch_bounds__(256) row_norm_scalar_kernel(RowArgs<T> a) {
+  using S = Scalar<T>;
+  __shared__ float partial[2][kWarpSize];
+  wait_for_upstream_grid();
+  release_downstream_grid();
+  const float n = static_cast<float>(a.hidden);
+  int parity = 0;
+  for (int64_t row = blockIdx.x; row < a.rows; row += gridDim.x) {
+    const int64_t base = row * a.hidden;
+    float sum_sq = 0.0f;
+    for (int c = threadIdx.x; c < a.hidden; c += blockDim.x) {
+      float v = S::load(a.input + base + c);
+      if constexpr (kAdd) {
+        v = S::round(__fadd_rn(v, S::load(a.residual + base + c)));
+        S::store(a.residual_output + base + c, v);
+      }
+      sum_sq = __fadd_rn(sum_sq, __fmul_rn(v, v));
+    }
+    const float inv = inverse_rms(block_allreduce_sum(sum_sq, partial, parity), n, a.epsilon);
+    parity ^= 1;
+    const T* source = kAdd ? a.residual_output : a.input;
+    for (int c = threadIdx.x; c < a.hidden; c += blockDim.x) {
+      const float v = S::load(source + base + c);
+      S::store(a.output + base + c, __fmul_rn(__fmul_rn(v, inv), S::load(a.weight + c)));
+    }
+  }
+}
+
+// ---------------------------------------------------------------------------
+// Host-side dispatch
+// ---------------------------------------------------------------------------
+enum class Family { kAuto, kWarp, kCta, kCtaOnePack, kWide, kScalar };
+
+// A persistent grid: enough blocks for `units` (rows / rows-per-block) but no
+// more than fit on the device at once.
+template <typename Kernel>
+int persistent_grid(Kernel kernel, int threads, int64_t blocks_needed, int* grid) {
+  DeviceInfo dev;
+  int rc = current_device_info(&dev);
+  if (rc != SM120N_OK) return rc;
+  int resident = 1;
+  rc = max_resident_ctas(reinterpret_cast<const void*>(kernel), threads, 0, &resident);
+  if (rc != SM120N_OK) return rc;
+  const int64_t cap = static_cast<int64_t>(dev.sm_count) * resident;
+  *grid = static_cast<int>(std::max<int64_t>(1, std::min<int64_t>(blocks_needed, cap)));
+  return SM120N_OK;
+}
+
+template <typename T, bool kAdd, int kPacksPerLane>
+int launch_warp(const RowArgs<T>& a, cudaStream_t stream) {
+  constexpr int kWarpsPerBlock = 4;
+  auto kernel = row_norm_warp_kernel<T, kAdd, kPacksPerLane>;
+  const int threads = kWarpsPerBlock * kWarpSize;
+  int grid = 0;
+  int rc = persistent_grid(kernel, threads, (a.rows + kWarpsPerBlock - 1) / kWarpsPerBlock, &grid);
+  if (rc != SM120N_OK) return rc;
+  return launch(kernel, dim3(grid), dim3(threads), 0, stream, a);
+}
+
+template <typename T, bool kAdd, int kPacksPerThread, int kMaxThreads>
+int launch_cta(const RowArgs<T>& a, int threads, cudaStream_t stream) {
+  auto kernel = row_norm_cta_kernel<T, kAdd, kPacksPerThread, kMaxThreads>;
+  int grid = 0;
+  int rc = persistent_grid(kernel, threads, a.rows, &grid);
+  if (rc != SM120N_OK) return rc;
+  return launch(kernel, dim3(grid), dim3(threads), 0, stream, a);
+}
+
+inline int round_up_warps(int64_t threads) {
+  return static_cast<int>((threads + kWarpSize - 1) / kWarpSize * kWarpSize);
+}
+
+template <typename T, bool kAdd>
+int run_rows(const RowArgs<T>& a, Family family, cudaStream_t stream) {
+  constexpr int E = Pack<T>::kElems;
+  const bool vectorisable =
+      a.hidden % E == 0 && aligned16(a.input) && aligned16(a.weight) && aligned16(a.output) &&
+      (!kAdd || (aligned16(a.residual) && aligned16(a.residual_output)));
+  const int packs = a.hidden / E;
+  if (!vectorisable) family = Family::kScalar;
+
+  if (family == Family::kAuto) {
+    family = packs <= 4 * kWarpSize ? Family::kWarp
+             : packs <= 1024        ? Family::kCta
+                                    : Family::kWide;
+  }
+  if (family == Family::kWarp && packs > 8 * kWarpSize) family = Family::kCta;
+  if ((family == Family::kCta || family == Family::kCtaOnePack) && packs > 1024) {
+    family = Family::kWide;
+  }
+
+  switch (family) {
+    case Family::kWarp:
+      if (packs <= 1 * kWarpSize) return launch_warp<T, kAdd, 1>(a, stream);
+      if (packs <= 2 * kWarpSize) return launch_warp<T, kAdd, 2>(a, stream);
+      if (packs <= 4 * kWarpSize) return launch_warp<T, kAdd, 4>(a, stream);
+      return launch_warp<T, kAdd, 8>(a, stream);
+    case Family::kCtaOnePack:
+      return launch_cta<T, kAdd, 1, 1024>(a, round_up_warps(packs), stream);
+    case Family::kCta: {
+      // Two packs per thread up to 512 threads keeps 32+ bytes of loads in
+      // flight per thread with a modest register budget.
+      if (packs <= 2 * 512) return launch_cta<T, kAdd, 2, 512>(a, round_up_warps((packs + 1) / 2), stream);
+      return launch_cta<T, kAdd, 4, 256>(a, round_up_warps((packs + 3) / 4), stream);
+    }
+    case Family::kWide: {
+      auto kernel = row_norm_wide_kernel<T, kAdd>;
+      const int threads = 1024;
+      int grid = 0;
+      int rc = persistent_grid(kernel, threads, a.rows, &grid);
+      if (rc != SM120N_OK) return rc;
+      return launch(kernel, dim3(grid), dim3(threads), 0, stream, a);
+    }
+    case Family::kScalar:
+    default: {
+      auto kernel = row_norm_scalar_kernel<T, kAdd>;
+      const int threads = 256;
+      int grid = 0;
+      int rc = persistent_grid(kernel, threads, a.rows, &grid);
+      if (rc != SM120N_OK) return rc;
+      return launch(kernel, dim3(grid), dim3(threads), 0, stream, a);
+    }
+  }
+}
+
+template <bool kAdd>
+int run_rows_typed(int dtype, const void* input, const void* residual, const void* weight,
+                   void* output, void* residual_output, int64_t rows, int64_t hidden,
+                   float epsilon, Family family, cudaStream_t stream) {
+  switch (dtype) {
+    case SM120N_F32: {
+      RowArgs<float> a{static_cast<const float*>(input), static_cast<const float*>(residual),
+                       static_cast<const float*>(weight), static_cast<float*>(output),
+                       static_cast<float*>(residual_output), rows, static_cast<int>(hidden),
+                       epsilon};
+      return run_rows<float, kAdd>(a, family, stream);
+    }
+    case SM120N_F16: {
+      RowArgs<__half> a{static_cast<const __half*>(input), static_cast<const __half*>(residual),
+                        static_cast<const __half*>(weight), static_cast<__half*>(output),
+                        static_cast<__half*>(residual_output), rows, static_cast<int>(hidden),
+                        epsilon};
+      return run_rows<__half, kAdd>(a, family, stream);
+    }
+    default: {
+      using B = __nv_bfloat16;
+      RowArgs<B> a{static_cast<const B*>(input), static_cast<const B*>(residual),
+                   static_cast<const B*>(weight), static_cast<B*>(output),
+                   static_cast<B*>(residual_output), rows, static_cast<int>(hidden), epsilon};
+      return run_rows<B, kAdd>(a, family, stream);
+    }
+  }
+}
+
+int check_rows(int64_t rows, int64_t hidden, int dtype) {
+  if (dtype_size(dtype) == 0) {
+    return fail(SM120N_ERR_INVALID_ARGUMENT, "supported dtypes are float16, bfloat16, and float32");
+  }
+  if (rows < 0) return fail(SM120N_ERR_INVALID_ARGUMENT, "rows must be non-negative (got %lld)",
+                            static_cast<long long>(rows));
+  if (hidden <= 0 || hidden > (int64_t{1} << 30)) {
+    return fail(SM120N_ERR_INVALID_ARGUMENT, "hidden_size must be in [1, 2^30] (got %lld)",
+                static_cast<long long>(hidden));
+  }
+  return SM120N_OK;
+}
+
+}  // namespace
+}  // namespace sm120n
+
+using namespace sm120n;
+
+extern "C" int sm120n_rms_norm(const void* input, const void* weight, void* output, int64_t rows,
+                               int64_t hidden_size, int dtype, float epsilon, int version,
+                               void* stream) {
+  clear_error();
+  int rc = check_rows(rows, hidden_size, dtype);
+  if (rc != SM120N_OK) return rc;
+  if (version != 1 && version != 2) {
+    return fail(SM120N_ERR_INVALID_ARGUMENT, "RMSNorm version must be 1 or 2");
+  }
+  if (rows == 0) return SM120N_OK;
+  if (!input || !weight || !output) {
+    return fail(SM120N_ERR_INVALID_ARGUMENT, "input, weight and output must be non-null");
+  }
+  const Family family = version == 1 ? Family::kCta : Family::kAuto;
+  return run_rows_typed<false>(dtype, input, nullptr, weight, output, nullptr, rows, hidden_size,
+                               epsilon, family, static_cast<cudaStream_t>(stream));
+}
+
+extern "C" int sm120n_fused_add_rms_norm(const void* input, const void* residual,
+                                         const void* weight, void* output, void* residual_output,
+                                         int64_t rows, int64_t hidden_size, int dtype,
+                                         float epsilon, int version, void* stream) {
+  clear_error();
+  int rc = check_rows(rows, hidden_size, dtype);
+  if (rc != SM120N_OK) return rc;
+  if (version < 0 || version > 4 || version == 1) {
+    return fail(SM120N_ERR_INVALID_ARGUMENT, "fused version must be 0 (auto), 2, 3, or 4");
+  }
+  if (version == 3 && hidden_size != 1024) {
+    return fail(SM120N_ERR_UNSUPPORTED, "V3 is specialized for hidden_size=1024");
+  }
+  if (version == 4 && hidden_size != 1024) {
+    return fail(SM120N_ERR_UNSUPPORTED, "V4 is specialized for hidden_size=1024");
+  }
+  if (rows == 0) return SM120N_OK;
+  if (!input || !residual || !weight || !output || !residual_output) {
+    return fail(SM120N_ERR_INVALID_ARGUMENT,
+                "input, residual, weight, output and residual_output must be non-null");
+  }
+  Family family = Family::kAuto;
+  switch (version) {
+    case 2: family = Family::kCta; break;
+    case 3: family = Family::kWarp; break;
+    case 4: family = Family::kCtaOnePack; break;
+    default: break;
+  }
+  return run_rows_typed<true>(dtype, input, residual, weight, output, residual_output, rows,
+                              hidden_size, epsilon, family, static_cast<cudaStream_t>(stream));
+}
+
+extern "C" int sm120n_get_device_faults(uint32_t* out_count) {
+  clear_error();
+  if (out_count == nullptr) return fail(SM120N_ERR_INVALID_ARGUMENT, "out_count must be non-null");
+  unsigned int value = 0;
+  const cudaError_t err = cudaMemcpyFromSymbol(&value, g_expired_waits, sizeof value);
+  if (err != cudaSuccess) {
+    return fail(SM120N_ERR_CUDA, "reading the fault counter failed: %s", cudaGetErrorString(err));
+  }
+  *out_count = value;
+  return SM120N_OK;
+}
+
+extern "C" int sm120n_reset_device_faults(void) {
+  clear_error();
+  const unsigned int zero = 0;
+  const cudaError_t err = cudaMemcpyToSymbol(g_expired_waits, &zero, sizeof zero);
+  if (err != cudaSuccess) {
+    return fail(SM120N_ERR_CUDA, "resetting the fault counter failed: %s", cudaGetErrorString(err));
+  }
+  return SM120N_OK;
+}

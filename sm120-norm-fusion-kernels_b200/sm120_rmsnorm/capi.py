@@ -1,0 +1,117 @@
+"""ctypes binding of the C ABI in ``include/sm120norm_b200.h``.
+
+For callers that hold raw device pointers (another runtime, another language's
+FFI, a custom allocator) rather than PyTorch tensors. Every function takes
+integer device addresses, sizes and a ``cudaStream_t`` as an integer (0 = the
+legacy default stream) and raises :class:`CApiError` on a non-zero status.
+The library is loaded from this package directory.
+"""
+from __future__ import annotations
+
+import ctypes
+import threading
+from pathlib import Path
+
+LIBRARY_NAME = "libsm120norm_b200.so"
+LIBRARY_PATH = Path(__file__).resolve().parent / LIBRARY_NAME
+
+F32, F16, BF16 = 0, 1, 2
+OK, ERR_INVALID_ARGUMENT, ERR_UNSUPPORTED, ERR_CUDA = 0, 1, 2, 3
+
+# Every symbol include/sm120norm_b200.h declares, with its ctypes signature.
+_i64, _i32, _f32, _vp = ctypes.c_int64, ctypes.c_int, ctypes.c_float, ctypes.c_void_p
+SIGNATURES: dict[str, tuple[list, object]] = {
+    "sm120n_abi_version": ([], _i32),
+    "sm120n_last_error": ([], ctypes.c_char_p),
+    "sm120n_status_string": ([_i32], ctypes.c_char_p),
+    "sm120n_set_programmatic_launch": ([_i32], None),
+    "sm120n_get_programmatic_launch": ([], _i32),
+    "sm120n_get_device_faults": ([ctypes.POINTER(ctypes.c_uint32)], _i32),
+    "sm120n_reset_device_faults": ([], _i32),
+    "sm120n_rms_norm": ([_vp, _vp, _vp, _i64, _i64, _i32, _f32, _i32, _vp], _i32),
+    "sm120n_fused_add_rms_norm": ([_vp, _vp, _vp, _vp, _vp, _i64, _i64, _i32, _f32, _i32, _vp], _i32),
+    "sm120n_fused_qk_rms_norm_rope": (
+        [_vp, _vp, _vp, _vp, _vp, _vp, _i64, _i64, _i64, _i64, _i64, _i32, _f32, _i32, _vp], _i32),
+    "sm120n_fused_qk_rms_norm_rope_kv": (
+        [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp,
+         _i64, _i64, _i64, _i64, _i64, _i64, _i32, _f32, _i32, _vp], _i32),
+}
+
+
+class CApiError(RuntimeError):
+    def __init__(self, status: int, message: str):
+        super().__init__(message or f"status {status}")
+        self.status = status
+
+
+_lock = threading.Lock()
+_lib: ctypes.CDLL | None = None
+
+
+def load(path: str | Path | None = None) -> ctypes.CDLL:
+    """Load (once) and return the shared library with typed signatures."""
+    global _lib
+    with _lock:
+        if _lib is None or path is not None:
+            lib = ctypes.CDLL(str(path or LIBRARY_PATH))
+            for name, (argtypes, restype) in SIGNATURES.items():
+                fn = getattr(lib, name)
+                fn.argtypes = argtypes
+                fn.restype = restype
+            _lib = lib
+    return _lib
+
+
+def _check(status: int) -> None:
+    if status != OK:
+        raise CApiError(status, load().sm120n_last_error().decode())
+
+
+def abi_version() -> int:
+    return load().sm120n_abi_version()
+
+
+def set_programmatic_launch(enabled: bool) -> None:
+    load().sm120n_set_programmatic_launch(1 if enabled else 0)
+
+
+def device_faults() -> int:
+    count = ctypes.c_uint32(0)
+    _check(load().sm120n_get_device_faults(ctypes.byref(count)))
+    return int(count.value)
+
+
+def reset_device_faults() -> None:
+    _check(load().sm120n_reset_device_faults())
+
+
+def rms_norm(input_ptr, weight_ptr, output_ptr, rows, hidden_size, dtype, epsilon=1e-6,
+             version=2, stream=0) -> None:
+    _check(load().sm120n_rms_norm(input_ptr, weight_ptr, output_ptr, rows, hidden_size, dtype,
+                                  epsilon, version, stream))
+
+
+def fused_add_rms_norm(input_ptr, residual_ptr, weight_ptr, output_ptr, residual_output_ptr,
+                       rows, hidden_size, dtype, epsilon=1e-6, version=0, stream=0) -> None:
+    _check(load().sm120n_fused_add_rms_norm(input_ptr, residual_ptr, weight_ptr, output_ptr,
+                                            residual_output_ptr, rows, hidden_size, dtype,
+                                            epsilon, version, stream))
+
+
+def fused_qk_rms_norm_rope(query_ptr, key_ptr, query_weight_ptr, key_weight_ptr, positions_ptr,
+                           cos_sin_ptr, tokens, query_heads, key_heads, head_dim,
+                           rope_positions, dtype, epsilon=1e-6, version=2, stream=0) -> None:
+    _check(load().sm120n_fused_qk_rms_norm_rope(
+        query_ptr, key_ptr, query_weight_ptr, key_weight_ptr, positions_ptr, cos_sin_ptr, tokens,
+        query_heads, key_heads, head_dim, rope_positions, dtype, epsilon, version, stream))
+
+
+def fused_qk_rms_norm_rope_kv(query_ptr, key_ptr, value_ptr, query_weight_ptr, key_weight_ptr,
+                              positions_ptr, cos_sin_ptr, key_cache_ptr, value_cache_ptr,
+                              slot_mapping_ptr, tokens, query_heads, key_heads, head_dim,
+                              rope_positions, cache_slots, dtype, epsilon=1e-6, version=1,
+                              stream=0) -> None:
+    _check(load().sm120n_fused_qk_rms_norm_rope_kv(
+        query_ptr, key_ptr, value_ptr, query_weight_ptr, key_weight_ptr, positions_ptr,
+        cos_sin_ptr, key_cache_ptr, value_cache_ptr, slot_mapping_ptr, tokens, query_heads,
+        key_heads, head_dim, rope_positions, cache_slots, dtype, epsilon, version, stream))
