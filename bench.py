@@ -139,6 +139,14 @@ def dram_traffic_per_launch():
     return out
 
 
+def sampled_gpus(world: int) -> str:
+    """nvidia-smi ids of the GPUs this job runs on."""
+    visible = os.environ.get("CUDA_VISIBLE_DEVICES")
+    if visible:
+        return ",".join(v.strip() for v in visible.split(",")[:world])
+    return ",".join(str(i) for i in range(world))
+
+
 class ClockSampler:
     """nvidia-smi samples of SM clock and throttle reasons during the timed region."""
 
@@ -152,6 +160,8 @@ class ClockSampler:
         self.lines: list[str] = []
 
     def __enter__(self):
+        if self.gpus is None:
+            return self
         cmd = ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
                "-lms", "100"]
         if self.gpus:
@@ -213,18 +223,32 @@ def event_pair():
     return torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
 
 
-def time_launches(fn, flush: Flusher, reps: int) -> float:
-    """Mean device time (us) of `fn`, each launch preceded by an L2 flush."""
-    times = []
+def capture(fns):
+    """A CUDA graph of the calls in `fns` (each run once first, so lazy kernel
+    loading stays out of it)."""
+    for fn in fns:
+        fn()
+    torch.cuda.synchronize()
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph):
+        for fn in fns:
+            fn()
+    return graph, []
+
+
+def time_graph(graph, flush: "Flusher", reps: int) -> float:
+    """Mean device time (us) of one replay, L2 flushed before every replay
+    (outside the timed events)."""
+    total = 0.0
     for _ in range(reps):
         flush()
         a, b = event_pair()
         a.record()
-        fn()
+        graph.replay()
         b.record()
         b.synchronize()
-        times.append(a.elapsed_time(b) * 1e3)
-    return statistics.fmean(times)
+        total += a.elapsed_time(b) * 1e3
+    return total / reps
 
 
 class SweepData:
@@ -265,8 +289,9 @@ def gpu_arm(args, dist: Dist) -> dict:
         graph.replay()
     dist.barrier()
     starts, ends = [], []
-    gpus = os.environ.get("CUDA_VISIBLE_DEVICES") if dist.world == 1 else None
-    with ClockSampler(gpus if dist.rank == 0 else "none") as clocks:
+    clocks = ClockSampler(sampled_gpus(dist.world) if dist.rank == 0 else None)
+    clocks.__enter__()
+    try:
         dist.barrier()
         for _ in range(args.steps):
             flush()
@@ -277,17 +302,37 @@ def gpu_arm(args, dist: Dist) -> dict:
             starts.append(a)
             ends.append(b)
         dist.barrier()
-    step_ms = sum(a.elapsed_time(b) for a, b in zip(starts, ends)) / args.steps
+        step_ms = sum(a.elapsed_time(b) for a, b in zip(starts, ends)) / args.steps
+        line = _measure_rest(args, dist, ops, flush, data, step_ms, launches_per_step)
+    finally:
+        clocks.__exit__(None, None, None)
+    line["clocks"] = clocks.summary() if dist.rank == 0 else None
+    return line
+
+
+def _measure_rest(args, dist, ops, flush, data, step_ms, launches_per_step) -> dict:
+    dev = torch.device("cuda", torch.cuda.current_device())
     step_ms_max = dist.max(step_ms)
     value = data.bytes * dist.world / (step_ms_max * 1e-3) / 1e9
 
-    # per-kernel launch durations (same shapes, each launch after a flush)
+    # per-launch durations: for each shape a graph of R back-to-back calls on
+    # R distinct buffer sets (every call reads data that is not in L2),
+    # replayed after an L2 flush; duration = replay time / R
     per_shape = []
+    g = torch.Generator(device="cuda").manual_seed(77 + dist.rank)
     for t, h, name, x, r, w in data.items:
-        us = time_launches(lambda: ops.fused_add_rms_norm_inplace(x, r, w, EPS), flush,
-                           max(3, args.reps))
+        nbytes = fused_bytes(t, h, x.element_size())
+        sets = max(1, min(64, (256 << 20) // nbytes))
+        bufs = [(x, r)] + [(torch.randn(t, h, device="cuda", generator=g).to(x.dtype),
+                            torch.randn(t, h, device="cuda", generator=g).to(x.dtype))
+                           for _ in range(sets - 1)]
+        calls = [(lambda bx=bx, br=br, w=w: ops.fused_add_rms_norm_inplace(bx, br, w, EPS))
+                 for bx, br in bufs]
+        shape_graph, _ = capture(calls)
+        us = time_graph(shape_graph, flush, max(3, args.reps)) / sets
+        del shape_graph, bufs, calls
         per_shape.append({"tokens": t, "hidden": h, "dtype": name, "us": round(dist.max(us), 3),
-                          "bytes": fused_bytes(t, h, x.element_size())})
+                          "bytes": nbytes, "calls_per_graph": sets})
     for p in per_shape:
         p["gbs"] = round(p["bytes"] / (p["us"] * 1e-6) / 1e9, 1)
     dominant = max(per_shape, key=lambda p: p["us"])
@@ -301,6 +346,8 @@ def gpu_arm(args, dist: Dist) -> dict:
                 "frac": round(dominant["gbs"] / peak, 4), "traffic": traffic_value,
                 "kernel": f"fused_add_rms_norm_inplace {dominant['dtype']} "
                           f"{dominant['tokens']}x{dominant['hidden']}",
+                "timing": "CUDA events around this call inside the step's graph, replayed "
+                          "after an L2 flush; mean over replays",
                 "algorithmic_bytes_per_launch": dominant["bytes"],
                 "launch_us": dominant["us"], "peak_source": peak_source + ", of measured"
                 if peak_source.startswith("measured") else peak_source + ", of fallback"}
@@ -335,7 +382,6 @@ def gpu_arm(args, dist: Dist) -> dict:
            "path": "sm120_rmsnorm.fused_add_rms_norm_inplace with pinned-host copies"}
 
     per_op = {} if args.skip_per_op else per_op_suite(ops, flush, dist, args)
-    clock = clocks.summary() if dist.rank == 0 else None
 
     return {
         "metric": "achieved HBM GB/s (% of B200 peak) and us/call per op at 1/2/4/8 GPUs",
@@ -352,16 +398,23 @@ def gpu_arm(args, dist: Dist) -> dict:
                    "l2": "flushed (512 MiB write) before every timed step and every "
                          "per-launch timing, outside the events"},
         "roofline": roofline, "e2e": e2e, "gpu_launches": launches_per_step * args.steps,
-        "clocks": clock, "per_shape": per_shape, "per_op": per_op,
+        "per_shape": per_shape, "per_op": per_op,
         "device": torch.cuda.get_device_name(dev),
     }
 
 
 def per_op_suite(ops, flush: Flusher, dist: Dist, args) -> dict:
-    """us/call and GB/s of each operator at the other workload shapes."""
+    """us/call and GB/s of each operator at the other workload shapes.
+
+    Each entry is a CUDA graph of R back-to-back calls on R distinct buffer
+    sets (R up to 64, fewer when a call moves more than 4 MiB), replayed after
+    an L2 flush, so every call reads inputs that are not in L2; us/call is the
+    replay time over R.
+    """
     out = {}
     reps = max(3, args.reps)
     g = torch.Generator(device="cuda").manual_seed(99 + dist.rank)
+    cpu_g = torch.Generator().manual_seed(7 + dist.rank)
     bf = torch.bfloat16
 
     def rope_cache(n):
@@ -371,53 +424,63 @@ def per_op_suite(ops, flush: Flusher, dist: Dist, args) -> dict:
 
     cache = rope_cache(32768)
 
-    def record(name, us, nbytes):
-        us = dist.max(us)
+    def sets_for(nbytes):
+        return max(1, min(64, (256 << 20) // max(nbytes, 1)))
+
+    def record(name, calls, nbytes):
+        graph, _ = capture(calls)
+        us = dist.max(time_graph(graph, flush, reps) / len(calls))
         out[name] = {"us": round(us, 3), "bytes": nbytes,
-                     "gbs": round(nbytes / (us * 1e-6) / 1e9, 1)}
+                     "gbs": round(nbytes / (us * 1e-6) / 1e9, 1), "calls_per_graph": len(calls)}
+        del graph
 
     # fp32 RMSNorm rows of 1024 (the CPU-runnable workload), on the GPU
     for t in (1, 4, 16, 64, 256):
-        x = torch.randn(t, 1024, device="cuda", generator=g)
-        w = 1.0 + 0.1 * torch.randn(1024, device="cuda", generator=g)
-        y = torch.empty_like(x)
-        record(f"rms_norm fp32 {t}x1024",
-               time_launches(lambda: ops.rms_norm_out(x, w, y, EPS), flush, reps),
-               rms_bytes(t, 1024, 4))
+        nbytes = rms_bytes(t, 1024, 4)
+        calls = []
+        for _ in range(sets_for(nbytes)):
+            x = torch.randn(t, 1024, device="cuda", generator=g)
+            w = 1.0 + 0.1 * torch.randn(1024, device="cuda", generator=g)
+            y = torch.empty_like(x)
+            calls.append(lambda x=x, w=w, y=y: ops.rms_norm_out(x, w, y, EPS))
+        record(f"rms_norm fp32 {t}x1024", calls, nbytes)
 
-    # Qwen3 decode QK norm + RoPE + paged KV store
-    def qk_case(name, b, hq, hk, blocks, positions, slots):
-        q = torch.randn(b, hq, 128, device="cuda", generator=g).to(bf)
-        k = torch.randn(b, hk, 128, device="cuda", generator=g).to(bf)
-        v = torch.randn(b, hk, 128, device="cuda", generator=g).to(bf)
-        qw = (1 + 0.1 * torch.randn(128, device="cuda", generator=g)).to(bf)
-        kw = (1 + 0.1 * torch.randn(128, device="cuda", generator=g)).to(bf)
+    # Qwen3 decode Q/K norm + RoPE + paged KV store (one cache per case,
+    # distinct slots and positions per buffer set)
+    def qk_case(name, b, hq, hk, blocks, contiguous):
+        nbytes = qk_kv_bytes(b, hq, hk, 2)
+        n_sets = sets_for(nbytes)
         kc = torch.zeros(blocks, 16, hk, 128, device="cuda", dtype=bf)
         vc = torch.zeros_like(kc)
-        fn = lambda: ops.fused_qk_rms_norm_rope_kv(q, k, v, qw, kw, positions, cache, kc, vc,
-                                                   slots, EPS)
-        record(name, time_launches(fn, flush, reps), qk_kv_bytes(b, hq, hk, 2))
-        del q, k, v, kc, vc
+        qw = (1 + 0.1 * torch.randn(128, device="cuda", generator=g)).to(bf)
+        kw = (1 + 0.1 * torch.randn(128, device="cuda", generator=g)).to(bf)
+        all_slots = torch.randperm(blocks * 16, generator=cpu_g)[: b * n_sets].to(torch.int32)
+        calls = []
+        for i in range(n_sets):
+            q = torch.randn(b, hq, 128, device="cuda", generator=g).to(bf)
+            k = torch.randn(b, hk, 128, device="cuda", generator=g).to(bf)
+            v = torch.randn(b, hk, 128, device="cuda", generator=g).to(bf)
+            if contiguous:
+                pos = torch.arange(b, device="cuda")
+                slots = torch.arange(b, device="cuda", dtype=torch.int32)
+            else:
+                pos = torch.randperm(32768, generator=cpu_g)[:b].cuda()
+                slots = all_slots[i * b:(i + 1) * b].cuda()
+            calls.append(lambda q=q, k=k, v=v, pos=pos, slots=slots: ops.fused_qk_rms_norm_rope_kv(
+                q, k, v, qw, kw, pos, cache, kc, vc, slots, EPS))
+        record(name, calls, nbytes)
 
-    cpu_g = torch.Generator().manual_seed(7 + dist.rank)
-    qk_case("qk_kv decode bf16 B=1 16/8", 1, 16, 8, 2048,
-            torch.randint(0, 32768, (1,), generator=cpu_g).cuda(),
-            torch.randint(0, 2048 * 16, (1,), generator=cpu_g).to(torch.int32).cuda())
+    qk_case("qk_kv decode bf16 B=1 16/8", 1, 16, 8, 2048, False)
     for b in (64, 256, 1024):
-        qk_case(f"qk_kv decode bf16 B={b} 32/8", b, 32, 8, 65536,
-                torch.randperm(32768, generator=cpu_g)[:b].cuda(),
-                torch.randperm(65536 * 16, generator=cpu_g)[:b].to(torch.int32).cuda())
-    qk_case("qk_kv prefill bf16 32768 tokens 64/8", 32768, 64, 8, 2048,
-            torch.arange(32768, device="cuda"),
-            torch.arange(32768, device="cuda", dtype=torch.int32))
+        qk_case(f"qk_kv decode bf16 B={b} 32/8", b, 32, 8, 65536, False)
+    qk_case("qk_kv prefill bf16 32768 tokens 64/8", 32768, 64, 8, 2048, True)
 
-    # prefill residual add + RMSNorm
+    # prefill residual add + RMSNorm (4.3 GB per call: one call per graph)
     x = torch.randn(65536, 8192, device="cuda", generator=g).to(bf)
     r = torch.randn(65536, 8192, device="cuda", generator=g).to(bf)
     w = (1 + 0.1 * torch.randn(8192, device="cuda", generator=g)).to(bf)
     record("fused_add_rms_norm_inplace prefill bf16 65536x8192",
-           time_launches(lambda: ops.fused_add_rms_norm_inplace(x, r, w, EPS), flush, reps),
-           fused_bytes(65536, 8192, 2))
+           [lambda: ops.fused_add_rms_norm_inplace(x, r, w, EPS)], fused_bytes(65536, 8192, 2))
     del x, r
     return out
 
@@ -493,6 +556,53 @@ def reference_arm(args, dist: Dist) -> dict:
 
 
 # ---------------------------------------------------------------------------
+def profile_case(args) -> None:
+    """Launch one operator at one shape `--launches` times (for ncu: skip the
+    first launches with -s and capture one with -c 1)."""
+    import sm120_rmsnorm as ops
+
+    torch.cuda.set_device(0)
+    dt = {"bf16": torch.bfloat16, "fp16": torch.float16, "fp32": torch.float32}[args.dtype]
+    g = torch.Generator(device="cuda").manual_seed(0)
+    t, h = args.tokens, args.hidden
+    if args.profile in ("fused", "rms"):
+        x = torch.randn(t, h, device="cuda", generator=g).to(dt)
+        r = torch.randn(t, h, device="cuda", generator=g).to(dt)
+        w = (1 + 0.1 * torch.randn(h, device="cuda", generator=g)).to(dt)
+        y = torch.empty_like(x)
+        if args.profile == "fused":
+            fn = lambda: ops.fused_add_rms_norm_inplace(x, r, w, EPS, args.version)
+        else:
+            fn = lambda: ops.rms_norm_out(x, w, y, EPS, args.version or 2)
+    else:
+        hq, hk = (int(v) for v in args.heads.split(","))
+        q = torch.randn(t, hq, 128, device="cuda", generator=g).to(dt)
+        k = torch.randn(t, hk, 128, device="cuda", generator=g).to(dt)
+        v = torch.randn(t, hk, 128, device="cuda", generator=g).to(dt)
+        qw = (1 + 0.1 * torch.randn(128, device="cuda", generator=g)).to(dt)
+        inv = 1.0 / (1e6 ** (torch.arange(0, 128, 2, dtype=torch.float32, device="cuda") / 128))
+        f = torch.outer(torch.arange(32768, dtype=torch.float32, device="cuda"), inv)
+        cache = torch.cat((f.cos(), f.sin()), dim=-1)
+        pos = torch.randint(0, 32768, (t,), device="cuda")
+        slots_total = max(t, 2048 * 16)
+        kc = torch.zeros(slots_total, hk, 128, device="cuda", dtype=dt)
+        vc = torch.zeros_like(kc)
+        slots = torch.randperm(slots_total, device="cuda")[:t].to(torch.int32)
+        if args.profile == "qkkv":
+            fn = lambda: ops.fused_qk_rms_norm_rope_kv(q, k, v, qw, qw, pos, cache, kc, vc, slots,
+                                                       EPS, args.version or 1)
+        else:
+            fn = lambda: ops.fused_qk_rms_norm_rope(q, k, qw, qw, pos, cache, EPS,
+                                                    args.version or 2)
+    flush = Flusher()
+    for _ in range(args.launches):
+        flush()
+        fn()
+    torch.cuda.synchronize()
+    print(f"profile: {args.profile} {args.dtype} tokens={t} hidden={h} heads={args.heads} "
+          f"launches={args.launches}")
+
+
 def main():
     parser = argparse.ArgumentParser(description=__doc__.splitlines()[0])
     parser.add_argument("--gpus", type=int, default=1)
@@ -503,7 +613,18 @@ def main():
     parser.add_argument("--cpu-seconds", type=float, default=10.0)
     parser.add_argument("--skip-per-op", action="store_true")
     parser.add_argument("--skip-cpu", action="store_true")
+    parser.add_argument("--profile", choices=["fused", "rms", "qkkv", "qk"],
+                        help="launch one operator at one shape and exit (ncu driver)")
+    parser.add_argument("--tokens", type=int, default=1024)
+    parser.add_argument("--hidden", type=int, default=4096)
+    parser.add_argument("--heads", default="32,8")
+    parser.add_argument("--dtype", default="bf16", choices=["bf16", "fp16", "fp32"])
+    parser.add_argument("--version", type=int, default=0)
+    parser.add_argument("--launches", type=int, default=5)
     args = parser.parse_args()
+    if args.profile:
+        profile_case(args)
+        return
     if args.warmup < 3:
         parser.error("--warmup must be at least 3")
 

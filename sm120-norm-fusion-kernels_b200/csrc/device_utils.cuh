@@ -162,4 +162,77 @@ __device__ __forceinline__ void release_downstream_grid() {
   asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
 }
 
+// ---------------------------------------------------------------------------
+// Bulk asynchronous copies (the TMA engine's untiled mode) into shared memory,
+// completion tracked by an mbarrier's transaction count. The source is always
+// this GPU's own global memory and each copy lands in the issuing CTA only.
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ uint32_t shared_address(const void* p) {
+  return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+
+__device__ __forceinline__ void mbarrier_init(uint64_t* bar, uint32_t arrivals) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(shared_address(bar)),
+               "r"(arrivals)
+               : "memory");
+}
+
+// Makes mbarrier initialisation visible to the asynchronous proxy.
+__device__ __forceinline__ void fence_mbarrier_init() {
+  asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+}
+
+// Orders this thread's earlier shared-memory accesses before later
+// asynchronous-proxy accesses (a bulk copy refilling a consumed stage).
+__device__ __forceinline__ void fence_async_shared() {
+  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+
+// One arrival that also announces `bytes` of incoming transactions.
+__device__ __forceinline__ void mbarrier_arrive_expect_tx(uint64_t* bar, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(shared_address(bar)),
+               "r"(bytes)
+               : "memory");
+}
+
+// `bytes` (a multiple of 16) from 16-byte-aligned global memory into
+// 16-byte-aligned shared memory; completes `bar`'s transactions.
+__device__ __forceinline__ void bulk_load(void* smem_dst, const void* gmem_src, uint32_t bytes,
+                                          uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::
+          "r"(shared_address(smem_dst)),
+      "l"(gmem_src), "r"(bytes), "r"(shared_address(bar))
+      : "memory");
+}
+
+__device__ __forceinline__ bool mbarrier_try_wait(uint64_t* bar, uint32_t parity) {
+  uint32_t done;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(done)
+      : "r"(shared_address(bar)), "r"(parity)
+      : "memory");
+  return done != 0;
+}
+
+// Every wait on asynchronous copies is bounded: after this many polls (each
+// poll may suspend the thread for a short hardware-defined time, so the bound
+// is tens of milliseconds or more, far beyond any real copy) the caller gets
+// `false` and must record a fault and stop instead of spinning forever.
+constexpr uint32_t kMaxBarrierPolls = 1u << 22;
+
+__device__ __forceinline__ bool mbarrier_wait_bounded(uint64_t* bar, uint32_t parity) {
+  for (uint32_t i = 0; i < kMaxBarrierPolls; ++i) {
+    if (mbarrier_try_wait(bar, parity)) return true;
+  }
+  return false;
+}
+
+__device__ __forceinline__ uint4 load16_shared(const void* p) {
+  return *reinterpret_cast<const uint4*>(p);
+}
+
 }  // namespace sm120n

@@ -58,52 +58,148 @@ struct HeadArgs {
   float epsilon;
 };
 
-// Eight consecutive elements as fp32: two 16-byte loads for fp32, one for
-// 16-bit types; element at a time when kVector is false (unaligned buffers).
-template <typename T, bool kVector>
-__device__ __forceinline__ void load8(const T* p, float* f) {
-  if constexpr (kVector) {
-    using P = Pack<T>;
-#pragma unroll
-    for (int i = 0; i < kElemsPerHalf / P::kElems; ++i) P::to_f32(load16(p + i * P::kElems), f + i * P::kElems);
-  } else {
-#pragma unroll
-    for (int i = 0; i < kElemsPerHalf; ++i) f[i] = Scalar<T>::load(p + i);
-  }
-}
-
-// Raw copy of eight elements (bit-exact V store).
-template <typename T, bool kVector>
-struct Raw8 {
-  static constexpr int kWords = kVector ? (kElemsPerHalf * sizeof(T) / 16) : kElemsPerHalf;
-  using Word = typename std::conditional<kVector, uint4, T>::type;
-  Word w[kWords];
-  __device__ __forceinline__ void load(const T* p) {
-#pragma unroll
-    for (int i = 0; i < kWords; ++i) w[i] = reinterpret_cast<const Word*>(p)[i];
-  }
-  __device__ __forceinline__ void store(T* p) const {
-#pragma unroll
-    for (int i = 0; i < kWords; ++i) reinterpret_cast<Word*>(p)[i] = w[i];
-  }
+// Eight elements of T as 32-bit words: four words (two elements each) for
+// 16-bit types, eight for fp32. Loaded with 16-byte accesses when the buffers
+// are aligned (kVector), element at a time otherwise.
+template <typename T>
+struct Half8 {
+  static constexpr int kWords = kElemsPerHalf * sizeof(T) / 4;
+  uint32_t w[kWords];
 };
 
-// Eight fp32 values rounded to T and stored; `bits` keeps the stored
-// encoding so the KV-cache copy is the identical bit pattern.
 template <typename T, bool kVector>
-__device__ __forceinline__ void store8(T* p, const float* f) {
+__device__ __forceinline__ Half8<T> load_half(const T* p) {
+  Half8<T> h;
   if constexpr (kVector) {
-    using P = Pack<T>;
 #pragma unroll
-    for (int i = 0; i < kElemsPerHalf / P::kElems; ++i) store16(p + i * P::kElems, P::from_f32(f + i * P::kElems));
+    for (int i = 0; i < Half8<T>::kWords / 4; ++i) {
+      const uint4 v = load16(p + i * (16 / sizeof(T)));
+      h.w[4 * i] = v.x;
+      h.w[4 * i + 1] = v.y;
+      h.w[4 * i + 2] = v.z;
+      h.w[4 * i + 3] = v.w;
+    }
+  } else if constexpr (sizeof(T) == 4) {
+#pragma unroll
+    for (int i = 0; i < 8; ++i) h.w[i] = reinterpret_cast<const uint32_t*>(p)[i];
   } else {
+    const uint16_t* q = reinterpret_cast<const uint16_t*>(p);
 #pragma unroll
-    for (int i = 0; i < kElemsPerHalf; ++i) Scalar<T>::store(p + i, f[i]);
+    for (int i = 0; i < 4; ++i) h.w[i] = uint32_t(q[2 * i]) | (uint32_t(q[2 * i + 1]) << 16);
+  }
+  return h;
+}
+
+template <typename T, bool kVector>
+__device__ __forceinline__ void store_half(T* p, const Half8<T>& h) {
+  if constexpr (kVector) {
+#pragma unroll
+    for (int i = 0; i < Half8<T>::kWords / 4; ++i) {
+      store16(p + i * (16 / sizeof(T)),
+              make_uint4(h.w[4 * i], h.w[4 * i + 1], h.w[4 * i + 2], h.w[4 * i + 3]));
+    }
+  } else if constexpr (sizeof(T) == 4) {
+#pragma unroll
+    for (int i = 0; i < 8; ++i) reinterpret_cast<uint32_t*>(p)[i] = h.w[i];
+  } else {
+    uint16_t* q = reinterpret_cast<uint16_t*>(p);
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      q[2 * i] = static_cast<uint16_t>(h.w[i] & 0xffffu);
+      q[2 * i + 1] = static_cast<uint16_t>(h.w[i] >> 16);
+    }
   }
 }
 
-__device__ __forceinline__ void load8_f32(const float* p, float* f, bool vector) {
-  if (vector) {
+// Element e of a half as fp32.
+template <typename T>
+__device__ __forceinline__ void unpack_half(const Half8<T>& h, float* f) {
+  if constexpr (sizeof(T) == 4) {
+#pragma unroll
+    for (int i = 0; i < 8; ++i) f[i] = __uint_as_float(h.w[i]);
+  } else {
+#pragma unroll
+    for (int i = 0; i < 4; ++i) Pack<T>::word_to_f32(h.w[i], f[2 * i], f[2 * i + 1]);
+  }
+}
+
+template <typename T>
+__device__ __forceinline__ Half8<T> pack_half(const float* f) {
+  Half8<T> h;
+  if constexpr (sizeof(T) == 4) {
+#pragma unroll
+    for (int i = 0; i < 8; ++i) h.w[i] = __float_as_uint(f[i]);
+  } else {
+#pragma unroll
+    for (int i = 0; i < 4; ++i) h.w[i] = Pack<T>::f32_to_word(f[2 * i], f[2 * i + 1]);
+  }
+  return h;
+}
+
+// Round-to-nearest-even product of two packed pairs. For bf16 and fp16 the
+// fp32 product of two such values is exact, so this single rounding equals
+// the oracle's round(round_fp32(n * w)).
+template <typename T>
+__device__ __forceinline__ uint32_t mul_pair_rn(uint32_t a, uint32_t b);
+template <>
+__device__ __forceinline__ uint32_t mul_pair_rn<__nv_bfloat16>(uint32_t a, uint32_t b) {
+  __nv_bfloat162 r = __hmul2_rn(*reinterpret_cast<__nv_bfloat162*>(&a),
+                                *reinterpret_cast<__nv_bfloat162*>(&b));
+  return *reinterpret_cast<uint32_t*>(&r);
+}
+template <>
+__device__ __forceinline__ uint32_t mul_pair_rn<__half>(uint32_t a, uint32_t b) {
+  __half2 r = __hmul2_rn(*reinterpret_cast<__half2*>(&a), *reinterpret_cast<__half2*>(&b));
+  return *reinterpret_cast<uint32_t*>(&r);
+}
+
+// Sum of the squares of a half. For 16-bit types x^2 is exact in fp32, so an
+// FMA equals the oracle's rounded square followed by a rounded add.
+template <typename T>
+__device__ __forceinline__ float half_sum_squares(const Half8<T>& h, float acc) {
+  float f[kElemsPerHalf];
+  unpack_half<T>(h, f);
+#pragma unroll
+  for (int i = 0; i < kElemsPerHalf; ++i) {
+    acc = sizeof(T) == 2 ? __fmaf_rn(f[i], f[i], acc) : __fadd_rn(acc, __fmul_rn(f[i], f[i]));
+  }
+  return acc;
+}
+
+// n = round(round(x * inv) * w), the RMSNorm rounded to T and then weighted
+// in T (reference.py:38-41).
+template <typename T>
+__device__ __forceinline__ Half8<T> normalise_half(const Half8<T>& x, const Half8<T>& w,
+                                                   float inv) {
+  Half8<T> n;
+  if constexpr (sizeof(T) == 4) {
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      n.w[i] = __float_as_uint(
+          __fmul_rn(__fmul_rn(__uint_as_float(x.w[i]), inv), __uint_as_float(w.w[i])));
+    }
+  } else {
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      float a, b;
+      Pack<T>::word_to_f32(x.w[i], a, b);
+      n.w[i] = mul_pair_rn<T>(Pack<T>::f32_to_word(__fmul_rn(a, inv), __fmul_rn(b, inv)), w.w[i]);
+    }
+  }
+  return n;
+}
+
+template <typename T>
+__device__ __forceinline__ Half8<T> select_half(bool first, const Half8<T>& a, const Half8<T>& b) {
+  Half8<T> r;
+#pragma unroll
+  for (int i = 0; i < Half8<T>::kWords; ++i) r.w[i] = first ? a.w[i] : b.w[i];
+  return r;
+}
+
+template <bool kVector>
+__device__ __forceinline__ void load8_f32(const float* p, float* f) {
+  if constexpr (kVector) {
     const float4 a = *reinterpret_cast<const float4*>(p);
     const float4 b = *reinterpret_cast<const float4*>(p + 4);
     f[0] = a.x; f[1] = a.y; f[2] = a.z; f[3] = a.w;
@@ -115,8 +211,7 @@ __device__ __forceinline__ void load8_f32(const float* p, float* f, bool vector)
 }
 
 template <typename T, bool kStoreKV, bool kVector>
-__global__ void __launch_bounds__(256) head_norm_rope_kernel(HeadArgs<T> a) {
-  using S = Scalar<T>;
+__global__ void __launch_bounds__(256, sizeof(T) == 2 ? 4 : 2) head_norm_rope_kernel(HeadArgs<T> a) {
   wait_for_upstream_grid();
   release_downstream_grid();
   const int lane = threadIdx.x & (kWarpSize - 1);
@@ -124,89 +219,82 @@ __global__ void __launch_bounds__(256) head_norm_rope_kernel(HeadArgs<T> a) {
   const int head_in_warp = lane / kLanesPerHead;
   const int lo = part * kElemsPerHalf;         // first-half elements [lo, lo + 8)
   const int hi = kHalf + lo;                   // partners            [hi, hi + 8)
-  const int64_t warp = (static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x) / kWarpSize;
-  const int64_t warps = (static_cast<int64_t>(gridDim.x) * blockDim.x) / kWarpSize;
-  const int heads = a.query_heads + a.key_heads;
-  const int64_t units = a.tokens * heads;
+  // The host splits launches so that tokens * heads < 2^31: unit indices fit
+  // in 32 bits and the token of a unit is one 32-bit division.
+  const uint32_t heads = static_cast<uint32_t>(a.query_heads + a.key_heads);
+  const uint32_t units = static_cast<uint32_t>(a.tokens) * heads;
+  const uint32_t warp = (blockIdx.x * blockDim.x + threadIdx.x) / kWarpSize;
+  const uint32_t warps = (gridDim.x * blockDim.x) / kWarpSize;
 
-  float qw_lo[kElemsPerHalf], qw_hi[kElemsPerHalf], kw_lo[kElemsPerHalf], kw_hi[kElemsPerHalf];
-  load8<T, kVector>(a.query_weight + lo, qw_lo);
-  load8<T, kVector>(a.query_weight + hi, qw_hi);
-  load8<T, kVector>(a.key_weight + lo, kw_lo);
-  load8<T, kVector>(a.key_weight + hi, kw_hi);
+  const Half8<T> qw_lo = load_half<T, kVector>(a.query_weight + lo);
+  const Half8<T> qw_hi = load_half<T, kVector>(a.query_weight + hi);
+  const Half8<T> kw_lo = load_half<T, kVector>(a.key_weight + lo);
+  const Half8<T> kw_hi = load_half<T, kVector>(a.key_weight + hi);
 
-  for (int64_t first = warp * kHeadsPerWarp; first < units; first += warps * kHeadsPerWarp) {
-    const int64_t unit = first + head_in_warp;
+  for (uint32_t first = warp * kHeadsPerWarp; first < units; first += warps * kHeadsPerWarp) {
+    const uint32_t unit = first + head_in_warp;
     const bool active = unit < units;
-    const int64_t token = active ? unit / heads : 0;
+    const uint32_t token = active ? unit / heads : 0;
     const int h = active ? static_cast<int>(unit - token * heads) : 0;
     const bool is_query = h < a.query_heads;
     const int kv_head = h - a.query_heads;
-    T* head = is_query ? a.query + (token * a.query_heads + h) * kHeadDim
-                       : a.key + (token * a.key_heads + kv_head) * kHeadDim;
+    T* head = is_query ? a.query + (static_cast<int64_t>(token) * a.query_heads + h) * kHeadDim
+                       : a.key + (static_cast<int64_t>(token) * a.key_heads + kv_head) * kHeadDim;
 
-    float x_lo[kElemsPerHalf], x_hi[kElemsPerHalf];
+    Half8<T> x_lo{}, x_hi{}, v_lo, v_hi;
     int64_t position = -1;
     int64_t slot = -1;
-    Raw8<T, kVector> v_lo, v_hi;
     if (active) {
-      load8<T, kVector>(head + lo, x_lo);
-      load8<T, kVector>(head + hi, x_hi);
+      x_lo = load_half<T, kVector>(head + lo);
+      x_hi = load_half<T, kVector>(head + hi);
       position = a.positions[token];
       if constexpr (kStoreKV) {
         if (!is_query) {
           slot = a.slots[token];
           if (slot >= 0 && slot < a.cache_slots) {
-            const T* vh = a.value + (token * a.key_heads + kv_head) * kHeadDim;
-            v_lo.load(vh + lo);
-            v_hi.load(vh + hi);
+            const T* vh = a.value + (static_cast<int64_t>(token) * a.key_heads + kv_head) * kHeadDim;
+            v_lo = load_half<T, kVector>(vh + lo);
+            v_hi = load_half<T, kVector>(vh + hi);
           } else {
             slot = -1;
           }
         }
       }
-    } else {
-#pragma unroll
-      for (int i = 0; i < kElemsPerHalf; ++i) x_lo[i] = x_hi[i] = 0.0f;
     }
 
-    float sum_sq = accumulate_squares(0.0f, x_lo, kElemsPerHalf);
-    sum_sq = accumulate_squares(sum_sq, x_hi, kElemsPerHalf);
+    float sum_sq = half_sum_squares<T>(x_hi, half_sum_squares<T>(x_lo, 0.0f));
     sum_sq = group_allreduce_sum<kLanesPerHead>(sum_sq);
     if (!active || position < 0 || position >= a.rope_positions) continue;
-    const float inv = inverse_rms(sum_sq, static_cast<float>(kHeadDim), a.epsilon);
+    // mean over 128 elements: a multiply by an exact power of two
+    const float inv = __fdiv_rn(
+        1.0f, __fsqrt_rn(__fadd_rn(__fmul_rn(sum_sq, 1.0f / kHeadDim), a.epsilon)));
 
-    // n = round(round(x * inv) * w): RMSNorm rounded to the activation dtype,
-    // then the weight multiply in that dtype (reference.py:38-41).
-    float n_lo[kElemsPerHalf], n_hi[kElemsPerHalf];
-#pragma unroll
-    for (int i = 0; i < kElemsPerHalf; ++i) {
-      const float w_lo = is_query ? qw_lo[i] : kw_lo[i];
-      const float w_hi = is_query ? qw_hi[i] : kw_hi[i];
-      n_lo[i] = S::round(__fmul_rn(S::round(__fmul_rn(x_lo[i], inv)), w_lo));
-      n_hi[i] = S::round(__fmul_rn(S::round(__fmul_rn(x_hi[i], inv)), w_hi));
-    }
+    const Half8<T> n_lo = normalise_half<T>(x_lo, select_half<T>(is_query, qw_lo, kw_lo), inv);
+    const Half8<T> n_hi = normalise_half<T>(x_hi, select_half<T>(is_query, qw_hi, kw_hi), inv);
 
-    float c[kElemsPerHalf], s[kElemsPerHalf];
+    float c[kElemsPerHalf], s[kElemsPerHalf], p[kElemsPerHalf], q[kElemsPerHalf];
     const float* row = a.cos_sin + position * kHeadDim;
-    load8_f32(row + lo, c, kVector);
-    load8_f32(row + hi, s, kVector);
+    load8_f32<kVector>(row + lo, c);
+    load8_f32<kVector>(row + hi, s);
+    unpack_half<T>(n_lo, p);
+    unpack_half<T>(n_hi, q);
     float y_lo[kElemsPerHalf], y_hi[kElemsPerHalf];
 #pragma unroll
     for (int i = 0; i < kElemsPerHalf; ++i) {
-      y_lo[i] = __fsub_rn(__fmul_rn(n_lo[i], c[i]), __fmul_rn(n_hi[i], s[i]));
-      y_hi[i] = __fadd_rn(__fmul_rn(n_hi[i], c[i]), __fmul_rn(n_lo[i], s[i]));
+      y_lo[i] = __fsub_rn(__fmul_rn(p[i], c[i]), __fmul_rn(q[i], s[i]));
+      y_hi[i] = __fadd_rn(__fmul_rn(q[i], c[i]), __fmul_rn(p[i], s[i]));
     }
-    store8<T, kVector>(head + lo, y_lo);
-    store8<T, kVector>(head + hi, y_hi);
+    const Half8<T> out_lo = pack_half<T>(y_lo);
+    const Half8<T> out_hi = pack_half<T>(y_hi);
+    store_half<T, kVector>(head + lo, out_lo);
+    store_half<T, kVector>(head + hi, out_hi);
     if constexpr (kStoreKV) {
       if (slot >= 0) {
-        T* kc = a.key_cache + (slot * a.key_heads + kv_head) * kHeadDim;
-        T* vc = a.value_cache + (slot * a.key_heads + kv_head) * kHeadDim;
-        store8<T, kVector>(kc + lo, y_lo);  // same rounding -> same bits as K
-        store8<T, kVector>(kc + hi, y_hi);
-        v_lo.store(vc + lo);
-        v_hi.store(vc + hi);
+        const int64_t cache_head = (slot * a.key_heads + kv_head) * kHeadDim;
+        store_half<T, kVector>(a.key_cache + cache_head + lo, out_lo);  // same bits as K
+        store_half<T, kVector>(a.key_cache + cache_head + hi, out_hi);
+        store_half<T, kVector>(a.value_cache + cache_head + lo, v_lo);
+        store_half<T, kVector>(a.value_cache + cache_head + hi, v_hi);
       }
     }
   }
@@ -215,34 +303,51 @@ __global__ void __launch_bounds__(256) head_norm_rope_kernel(HeadArgs<T> a) {
 // threads_per_block == 0 selects the B200 default: up to 256 threads and a
 // persistent grid capped at what is resident on the device.
 template <typename T, bool kStoreKV>
-int run_heads(const HeadArgs<T>& a, int threads_per_block, cudaStream_t stream) {
+int run_heads(HeadArgs<T> a, int threads_per_block, cudaStream_t stream) {
   const bool vector = aligned16(a.query) && aligned16(a.key) && aligned16(a.query_weight) &&
                       aligned16(a.key_weight) && aligned16(a.cos_sin) &&
                       (!kStoreKV || (aligned16(a.value) && aligned16(a.key_cache) &&
                                      aligned16(a.value_cache)));
   auto kernel = vector ? head_norm_rope_kernel<T, kStoreKV, true>
                        : head_norm_rope_kernel<T, kStoreKV, false>;
-  const int64_t units = a.tokens * (a.query_heads + a.key_heads);
-  const int64_t warps_needed = (units + kHeadsPerWarp - 1) / kHeadsPerWarp;
-  int64_t threads = threads_per_block;
-  int64_t blocks;
-  if (threads == 0) {
-    threads = std::min<int64_t>(256, warps_needed * kWarpSize);
-    blocks = (warps_needed * kWarpSize + threads - 1) / threads;
-    DeviceInfo dev;
-    int rc = current_device_info(&dev);
+  const int64_t heads = a.query_heads + a.key_heads;
+  // Keep tokens * heads below 2^31 per launch (the kernel indexes units in
+  // 32 bits); larger calls become consecutive launches on the same stream.
+  const int64_t max_tokens = ((int64_t{1} << 31) - 1) / heads;
+  const int64_t all_tokens = a.tokens;
+  for (int64_t done = 0; done < all_tokens; done += max_tokens) {
+    HeadArgs<T> c = a;
+    c.tokens = std::min(max_tokens, all_tokens - done);
+    c.query = a.query + done * a.query_heads * kHeadDim;
+    c.key = a.key + done * a.key_heads * kHeadDim;
+    c.positions = a.positions + done;
+    if constexpr (kStoreKV) {
+      c.value = a.value + done * a.key_heads * kHeadDim;
+      c.slots = a.slots + done;
+    }
+    const int64_t units = c.tokens * heads;
+    const int64_t warps_needed = (units + kHeadsPerWarp - 1) / kHeadsPerWarp;
+    int64_t threads = threads_per_block;
+    int64_t blocks;
+    if (threads == 0) {
+      threads = std::min<int64_t>(256, warps_needed * kWarpSize);
+      blocks = (warps_needed * kWarpSize + threads - 1) / threads;
+      DeviceInfo dev;
+      int rc = current_device_info(&dev);
+      if (rc != SM120N_OK) return rc;
+      int resident = 1;
+      rc = max_resident_ctas(reinterpret_cast<const void*>(kernel), static_cast<int>(threads), 0,
+                             &resident);
+      if (rc != SM120N_OK) return rc;
+      blocks = std::min<int64_t>(blocks, static_cast<int64_t>(dev.sm_count) * resident);
+    } else {
+      blocks = (warps_needed * kWarpSize + threads - 1) / threads;
+    }
+    const int rc = launch(kernel, dim3(static_cast<unsigned>(std::max<int64_t>(blocks, 1))),
+                          dim3(static_cast<unsigned>(threads)), 0, stream, c);
     if (rc != SM120N_OK) return rc;
-    int resident = 1;
-    rc = max_resident_ctas(reinterpret_cast<const void*>(kernel), static_cast<int>(threads), 0,
-                           &resident);
-    if (rc != SM120N_OK) return rc;
-    blocks = std::min<int64_t>(blocks, static_cast<int64_t>(dev.sm_count) * resident);
-  } else {
-    blocks = (warps_needed * kWarpSize + threads - 1) / threads;
-    blocks = std::min<int64_t>(blocks, int64_t{1} << 30);
   }
-  return launch(kernel, dim3(static_cast<unsigned>(std::max<int64_t>(blocks, 1))),
-                dim3(static_cast<unsigned>(threads)), 0, stream, a);
+  return SM120N_OK;
 }
 
 template <bool kStoreKV>

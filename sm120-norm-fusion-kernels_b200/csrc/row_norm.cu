@@ -264,10 +264,144 @@ __global__ void __launch_bounds__(256) row_norm_scalar_kernel(RowArgs<T> a) {
   }
 }
 
+// ---- bulk family: rows staged through shared memory by the TMA engine ------
+// Persistent blocks; block b owns rows b, b + gridDim.x, ... and keeps up to
+// `stages` of them in flight. Thread 0 streams a row's input (and residual)
+// into a shared-memory stage with cp.async.bulk; the stage's mbarrier counts
+// the arriving bytes. Every thread waits for the stage, reads its 16-byte
+// packs from shared memory, and joins the block reduction; that barrier also
+// proves the stage has been read, so thread 0 refills it with the row
+// `stages` ahead before the outputs are computed and stored from registers.
+// Memory-level parallelism therefore comes from the copy engine, not from
+// registers held by waiting threads.
+constexpr int kMaxStages = 8;
+
+template <typename T, bool kAdd, int kPacksPerThread>
+__global__ void __launch_bounds__(1024) row_norm_bulk_kernel(RowArgs<T> a, int stages) {
+  constexpr int E = Pack<T>::kElems;
+  extern __shared__ __align__(128) unsigned char stage_memory[];
+  __shared__ __align__(8) uint64_t stage_full[kMaxStages];
+  __shared__ float partial[2][kWarpSize];
+  const int lane = threadIdx.x & (kWarpSize - 1);
+  const int warp = threadIdx.x / kWarpSize;
+  const int warps = blockDim.x / kWarpSize;
+  const int packs = a.hidden / E;
+  const uint32_t row_bytes = static_cast<uint32_t>(a.hidden) * sizeof(T);
+  const uint32_t stage_bytes = kAdd ? 2 * row_bytes : row_bytes;
+  const int64_t first_row = blockIdx.x;
+  const int64_t my_rows =
+      first_row < a.rows ? (a.rows - first_row + gridDim.x - 1) / gridDim.x : 0;
+  const float n = static_cast<float>(a.hidden);
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < stages; ++s) mbarrier_init(&stage_full[s], 1);
+    fence_mbarrier_init();
+  }
+  __syncthreads();
+  wait_for_upstream_grid();
+  release_downstream_grid();
+
+  auto refill = [&](int64_t i) {  // thread 0 only
+    const int s = static_cast<int>(i % stages);
+    const int64_t row = first_row + i * gridDim.x;
+    unsigned char* dst = stage_memory + static_cast<size_t>(s) * stage_bytes;
+    mbarrier_arrive_expect_tx(&stage_full[s], stage_bytes);
+    bulk_load(dst, a.input + row * a.hidden, row_bytes, &stage_full[s]);
+    if constexpr (kAdd) bulk_load(dst + row_bytes, a.residual + row * a.hidden, row_bytes, &stage_full[s]);
+  };
+  if (threadIdx.x == 0) {
+    for (int64_t i = 0; i < my_rows && i < stages; ++i) refill(i);
+  }
+
+  uint4 w[kPacksPerThread];
+#pragma unroll
+  for (int k = 0; k < kPacksPerThread; ++k) {
+    const int c = threadIdx.x + k * blockDim.x;
+    if (c < packs) w[k] = load16(a.weight + static_cast<int64_t>(c) * E);
+  }
+
+  for (int64_t i = 0; i < my_rows; ++i) {
+    const int s = static_cast<int>(i % stages);
+    const uint32_t phase = static_cast<uint32_t>((i / stages) & 1);
+    const bool arrived = mbarrier_wait_bounded(&stage_full[s], phase);
+    const unsigned char* stage = stage_memory + static_cast<size_t>(s) * stage_bytes;
+    uint4 v[kPacksPerThread];
+    float sum_sq = 0.0f;
+#pragma unroll
+    for (int k = 0; k < kPacksPerThread; ++k) {
+      const int c = threadIdx.x + k * blockDim.x;
+      if (c < packs) {
+        uint4 r;
+        if constexpr (kAdd) r = load16_shared(stage + row_bytes + static_cast<uint32_t>(c) * 16);
+        float f[E];
+        v[k] = combine<T, kAdd>(load16_shared(stage + static_cast<uint32_t>(c) * 16), r, f);
+        sum_sq = accumulate_squares(sum_sq, f, E);
+      }
+    }
+    sum_sq = group_allreduce_sum<kWarpSize>(sum_sq);
+    if (lane == 0) partial[i & 1][warp] = sum_sq;
+    if (__syncthreads_or(!arrived)) {
+      // A copy never completed within the bound: record it, give copies still
+      // in flight a bounded chance to land, and leave this block's rows.
+      if (threadIdx.x == 0) {
+        atomicAdd(&g_expired_waits, 1u);
+        for (int64_t j = i; j < my_rows && j < i + stages; ++j) {
+          mbarrier_wait_bounded(&stage_full[j % stages], static_cast<uint32_t>((j / stages) & 1));
+        }
+      }
+      __syncthreads();
+      return;
+    }
+    if (threadIdx.x == 0 && i + stages < my_rows) {
+      fence_async_shared();  // this stage's shared-memory reads before the refill
+      refill(i + stages);
+    }
+    float total = 0.0f;
+    for (int k = 0; k < warps; ++k) total = __fadd_rn(total, partial[i & 1][k]);
+    const float inv = inverse_rms(total, n, a.epsilon);
+    const int64_t base = (first_row + i * gridDim.x) * a.hidden;
+#pragma unroll
+    for (int k = 0; k < kPacksPerThread; ++k) {
+      const int c = threadIdx.x + k * blockDim.x;
+      if (c < packs) {
+        const int64_t off = base + static_cast<int64_t>(c) * E;
+        if constexpr (kAdd) store16(a.residual_output + off, v[k]);
+        store16(a.output + off, scale<T>(v[k], w[k], inv));
+      }
+    }
+  }
+}
+
 // ---------------------------------------------------------------------------
 // Host-side dispatch
 // ---------------------------------------------------------------------------
-enum class Family { kAuto, kWarp, kCta, kCtaOnePack, kWide, kScalar };
+enum class Family { kAuto, kWarp, kCta, kCtaOnePack, kWide, kBulk, kScalar };
+
+// Launch shape of the bulk family, or false when a row does not fit.
+struct BulkPlan {
+  int threads = 0;
+  int stages = 0;
+  size_t smem = 0;
+};
+
+inline bool plan_bulk(int64_t hidden, int elem_size, bool add, int packs_per_thread,
+                      size_t block_smem, BulkPlan* plan) {
+  const size_t row_bytes = static_cast<size_t>(hidden) * elem_size;
+  const size_t stage_bytes = add ? 2 * row_bytes : row_bytes;
+  const int64_t packs = row_bytes / 16;
+  const int64_t threads = (packs + packs_per_thread - 1) / packs_per_thread;
+  if (threads > 1024) return false;
+  // About 96 KiB of rows in flight per block, between 2 and 8 stages.
+  int stages = static_cast<int>(std::min<size_t>(kMaxStages, (96 * 1024) / stage_bytes));
+  stages = std::max(stages, 2);
+  const size_t static_smem = 1024;  // barriers and partial sums, rounded up
+  while (stages > 2 && stages * stage_bytes + static_smem > block_smem) --stages;
+  if (stages * stage_bytes + static_smem > block_smem) return false;
+  plan->threads = static_cast<int>((threads + kWarpSize - 1) / kWarpSize * kWarpSize);
+  plan->stages = stages;
+  plan->smem = stages * stage_bytes;
+  return true;
+}
 
 // A persistent grid: enough blocks for `units` (rows / rows-per-block) but no
 // more than fit on the device at once.
@@ -304,6 +438,23 @@ int launch_cta(const RowArgs<T>& a, int threads, cudaStream_t stream) {
   return launch(kernel, dim3(grid), dim3(threads), 0, stream, a);
 }
 
+template <typename T, bool kAdd, int kPacksPerThread>
+int launch_bulk(const RowArgs<T>& a, const BulkPlan& plan, cudaStream_t stream) {
+  auto kernel = row_norm_bulk_kernel<T, kAdd, kPacksPerThread>;
+  int rc = allow_dynamic_smem(reinterpret_cast<const void*>(kernel), plan.smem);
+  if (rc != SM120N_OK) return rc;
+  DeviceInfo dev;
+  rc = current_device_info(&dev);
+  if (rc != SM120N_OK) return rc;
+  int resident = 1;
+  rc = max_resident_ctas(reinterpret_cast<const void*>(kernel), plan.threads, plan.smem, &resident);
+  if (rc != SM120N_OK) return rc;
+  const int64_t grid = std::max<int64_t>(
+      1, std::min<int64_t>(a.rows, static_cast<int64_t>(dev.sm_count) * resident));
+  return launch(kernel, dim3(static_cast<unsigned>(grid)), dim3(plan.threads), plan.smem, stream,
+                a, plan.stages);
+}
+
 inline int round_up_warps(int64_t threads) {
   return static_cast<int>((threads + kWarpSize - 1) / kWarpSize * kWarpSize);
 }
@@ -318,9 +469,19 @@ int run_rows(const RowArgs<T>& a, Family family, cudaStream_t stream) {
   if (!vectorisable) family = Family::kScalar;
 
   if (family == Family::kAuto) {
-    family = packs <= 4 * kWarpSize ? Family::kWarp
-             : packs <= 1024        ? Family::kCta
-                                    : Family::kWide;
+    // Rows up to 2 KiB: a warp per row. Wider rows, when there are enough of
+    // them to keep every SM's copy pipeline busy: the bulk (TMA) family.
+    // Otherwise a block per row, or the two-pass kernel for very wide rows.
+    DeviceInfo dev;
+    int rc = current_device_info(&dev);
+    if (rc != SM120N_OK) return rc;
+    if (packs <= 4 * kWarpSize) {
+      family = Family::kWarp;
+    } else if (a.rows >= 2 * static_cast<int64_t>(dev.sm_count)) {
+      family = Family::kBulk;
+    } else {
+      family = packs <= 1024 ? Family::kCta : Family::kWide;
+    }
   }
   if (family == Family::kWarp && packs > 8 * kWarpSize) family = Family::kCta;
   if ((family == Family::kCta || family == Family::kCtaOnePack) && packs > 1024) {
@@ -340,6 +501,20 @@ int run_rows(const RowArgs<T>& a, Family family, cudaStream_t stream) {
       // flight per thread with a modest register budget.
       if (packs <= 2 * 512) return launch_cta<T, kAdd, 2, 512>(a, round_up_warps((packs + 1) / 2), stream);
       return launch_cta<T, kAdd, 4, 256>(a, round_up_warps((packs + 3) / 4), stream);
+    }
+    case Family::kBulk: {
+      size_t block_smem = 0;
+      int rc = max_block_smem(&block_smem);
+      if (rc != SM120N_OK) return rc;
+      BulkPlan plan;
+      if (plan_bulk(a.hidden, sizeof(T), kAdd, 2, block_smem, &plan)) {
+        return launch_bulk<T, kAdd, 2>(a, plan, stream);
+      }
+      if (plan_bulk(a.hidden, sizeof(T), kAdd, 4, block_smem, &plan)) {
+        return launch_bulk<T, kAdd, 4>(a, plan, stream);
+      }
+      family = Family::kWide;  // rows too wide to stage: two-pass kernel
+      [[fallthrough]];
     }
     case Family::kWide: {
       auto kernel = row_norm_wide_kernel<T, kAdd>;

@@ -20,6 +20,8 @@ constexpr int kMaxDevices = 64;
 std::mutex g_cache_mutex;
 int g_sm_count[kMaxDevices] = {0};
 std::map<std::tuple<int, const void*, int, size_t>, int> g_occupancy;
+std::map<std::pair<int, const void*>, size_t> g_smem_optin;
+size_t g_block_smem[kMaxDevices] = {0};
 
 }  // namespace
 
@@ -85,6 +87,48 @@ int max_resident_ctas(const void* kernel, int threads, size_t smem, int* out) {
   std::lock_guard<std::mutex> lock(g_cache_mutex);
   g_occupancy[key] = ctas;
   *out = ctas;
+  return SM120N_OK;
+}
+
+int allow_dynamic_smem(const void* kernel, size_t bytes) {
+  int device = 0;
+  cudaError_t err = cudaGetDevice(&device);
+  if (err != cudaSuccess) {
+    return fail(SM120N_ERR_CUDA, "cudaGetDevice failed: %s", cudaGetErrorString(err));
+  }
+  std::lock_guard<std::mutex> lock(g_cache_mutex);
+  size_t& granted = g_smem_optin[std::make_pair(device, kernel)];
+  if (granted >= bytes) return SM120N_OK;
+  err = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             static_cast<int>(bytes));
+  if (err != cudaSuccess) {
+    return fail(SM120N_ERR_CUDA, "cannot grant %zu bytes of shared memory: %s", bytes,
+                cudaGetErrorString(err));
+  }
+  granted = bytes;
+  return SM120N_OK;
+}
+
+int max_block_smem(size_t* bytes) {
+  int device = 0;
+  cudaError_t err = cudaGetDevice(&device);
+  if (err != cudaSuccess) {
+    return fail(SM120N_ERR_CUDA, "cudaGetDevice failed: %s", cudaGetErrorString(err));
+  }
+  if (device < 0 || device >= kMaxDevices) {
+    return fail(SM120N_ERR_UNSUPPORTED, "device ordinal %d is out of range", device);
+  }
+  std::lock_guard<std::mutex> lock(g_cache_mutex);
+  if (g_block_smem[device] == 0) {
+    int value = 0;
+    err = cudaDeviceGetAttribute(&value, cudaDevAttrMaxSharedMemoryPerBlockOptin, device);
+    if (err != cudaSuccess || value <= 0) {
+      return fail(SM120N_ERR_CUDA, "cannot query shared memory per block: %s",
+                  cudaGetErrorString(err));
+    }
+    g_block_smem[device] = static_cast<size_t>(value);
+  }
+  *bytes = g_block_smem[device];
   return SM120N_OK;
 }
 

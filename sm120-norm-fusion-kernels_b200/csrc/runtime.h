@@ -33,6 +33,13 @@ int current_device_info(DeviceInfo* info);
 // dynamic shared bytes on the current device (cached).
 int max_resident_ctas(const void* kernel, int threads, size_t smem, int* out);
 
+// Allows `kernel` to use `bytes` of dynamic shared memory on the current
+// device (cudaFuncAttributeMaxDynamicSharedMemorySize; cached).
+int allow_dynamic_smem(const void* kernel, size_t bytes);
+
+// Shared memory a block may use on the current device (opt-in maximum).
+int max_block_smem(size_t* bytes);
+
 // Launch `kernel` on `stream`, with the programmatic-stream-serialisation
 // attribute when enabled.
 template <typename... KernelArgs, typename... Args>
