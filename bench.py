@@ -346,8 +346,9 @@ def _measure_rest(args, dist, ops, flush, data, step_ms, launches_per_step) -> d
                 "frac": round(dominant["gbs"] / peak, 4), "traffic": traffic_value,
                 "kernel": f"fused_add_rms_norm_inplace {dominant['dtype']} "
                           f"{dominant['tokens']}x{dominant['hidden']}",
-                "timing": "CUDA events around this call inside the step's graph, replayed "
-                          "after an L2 flush; mean over replays",
+                "timing": "CUDA events around a graph of R back-to-back calls of this "
+                          "shape on R distinct buffer sets, replayed after an L2 flush; "
+                          "duration = replay time / R",
                 "algorithmic_bytes_per_launch": dominant["bytes"],
                 "launch_us": dominant["us"], "peak_source": peak_source + ", of measured"
                 if peak_source.startswith("measured") else peak_source + ", of fallback"}

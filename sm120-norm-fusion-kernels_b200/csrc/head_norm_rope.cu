@@ -273,9 +273,8 @@ __global__ void __launch_bounds__(256, sizeof(T) == 2 ? 4 : 2) head_norm_rope_ke
     const Half8<T> n_hi = normalise_half<T>(x_hi, select_half<T>(is_query, qw_hi, kw_hi), inv);
 
     float c[kElemsPerHalf], s[kElemsPerHalf], p[kElemsPerHalf], q[kElemsPerHalf];
-    const float* row = a.cos_sin + position * kHeadDim;
-    load8_f32<kVector>(row + lo, c);
-    load8_f32<kVector>(row + hi, s);
+    load8_f32<kVector>(a.cos_sin + position * kHeadDim + lo, c);
+    load8_f32<kVector>(a.cos_sin + position * kHeadDim + hi, s);
     unpack_half<T>(n_lo, p);
     unpack_half<T>(n_hi, q);
     float y_lo[kElemsPerHalf], y_hi[kElemsPerHalf];
@@ -308,9 +307,12 @@ int run_heads(HeadArgs<T> a, int threads_per_block, cudaStream_t stream) {
                       aligned16(a.key_weight) && aligned16(a.cos_sin) &&
                       (!kStoreKV || (aligned16(a.value) && aligned16(a.key_cache) &&
                                      aligned16(a.value_cache)));
+  const int64_t heads = a.query_heads + a.key_heads;
+  DeviceInfo dev;
+  int rc = current_device_info(&dev);
+  if (rc != SM120N_OK) return rc;
   auto kernel = vector ? head_norm_rope_kernel<T, kStoreKV, true>
                        : head_norm_rope_kernel<T, kStoreKV, false>;
-  const int64_t heads = a.query_heads + a.key_heads;
   // Keep tokens * heads below 2^31 per launch (the kernel indexes units in
   // 32 bits); larger calls become consecutive launches on the same stream.
   const int64_t max_tokens = ((int64_t{1} << 31) - 1) / heads;
@@ -332,9 +334,6 @@ int run_heads(HeadArgs<T> a, int threads_per_block, cudaStream_t stream) {
     if (threads == 0) {
       threads = std::min<int64_t>(256, warps_needed * kWarpSize);
       blocks = (warps_needed * kWarpSize + threads - 1) / threads;
-      DeviceInfo dev;
-      int rc = current_device_info(&dev);
-      if (rc != SM120N_OK) return rc;
       int resident = 1;
       rc = max_resident_ctas(reinterpret_cast<const void*>(kernel), static_cast<int>(threads), 0,
                              &resident);
@@ -343,8 +342,8 @@ int run_heads(HeadArgs<T> a, int threads_per_block, cudaStream_t stream) {
     } else {
       blocks = (warps_needed * kWarpSize + threads - 1) / threads;
     }
-    const int rc = launch(kernel, dim3(static_cast<unsigned>(std::max<int64_t>(blocks, 1))),
-                          dim3(static_cast<unsigned>(threads)), 0, stream, c);
+    rc = launch(kernel, dim3(static_cast<unsigned>(std::max<int64_t>(blocks, 1))),
+                dim3(static_cast<unsigned>(threads)), 0, stream, c);
     if (rc != SM120N_OK) return rc;
   }
   return SM120N_OK;

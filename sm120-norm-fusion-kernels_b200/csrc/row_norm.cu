@@ -13,9 +13,12 @@
 // and the measured occupancy. Kernel families:
 //
 //   warp   one warp per row, rows <= 32 * 8 packs (<= 4 KiB of bf16);
-//          shuffle-only reduction, no block barrier.
-//   cta    one thread block per row, rows <= 1024 packs (16 KiB of bf16);
-//          one barrier per row (double-buffered partial sums).
+//          shuffle-only reduction, no block barrier (fused version 3).
+//   cta    one thread block per row, rows <= 1024 packs (16 KiB of bf16),
+//          1, 2 or 4 packs per thread; one barrier per row (double-buffered
+//          partial sums). The default for every row up to 16 KiB.
+//   bulk   persistent blocks, rows staged through shared memory by the TMA
+//          engine (cp.async.bulk, mbarrier completion); rows of 16-32 KiB.
 //   wide   one thread block per row, any 16-byte-aligned row; two passes
 //          (the second re-reads the row, which is then L2-resident).
 //   scalar any row, any alignment; element at a time, two passes.
@@ -429,12 +432,20 @@ int launch_warp(const RowArgs<T>& a, cudaStream_t stream) {
   return launch(kernel, dim3(grid), dim3(threads), 0, stream, a);
 }
 
+// `one_row_per_block`: a block per row and let the block scheduler balance
+// the waves (best for many rows: measured 620 us vs 682 us persistent on the
+// 65536 x 8192 bf16 prefill); otherwise a persistent grid with a row loop.
 template <typename T, bool kAdd, int kPacksPerThread, int kMaxThreads>
-int launch_cta(const RowArgs<T>& a, int threads, cudaStream_t stream) {
+int launch_cta(const RowArgs<T>& a, int threads, cudaStream_t stream,
+               bool one_row_per_block = false) {
   auto kernel = row_norm_cta_kernel<T, kAdd, kPacksPerThread, kMaxThreads>;
   int grid = 0;
-  int rc = persistent_grid(kernel, threads, a.rows, &grid);
-  if (rc != SM120N_OK) return rc;
+  if (one_row_per_block && a.rows <= INT32_MAX) {
+    grid = static_cast<int>(a.rows);
+  } else {
+    int rc = persistent_grid(kernel, threads, a.rows, &grid);
+    if (rc != SM120N_OK) return rc;
+  }
   return launch(kernel, dim3(grid), dim3(threads), 0, stream, a);
 }
 
@@ -468,19 +479,28 @@ int run_rows(const RowArgs<T>& a, Family family, cudaStream_t stream) {
   const int packs = a.hidden / E;
   if (!vectorisable) family = Family::kScalar;
 
+  bool many_rows = false;
   if (family == Family::kAuto) {
-    // Rows up to 2 KiB: a warp per row. Wider rows, when there are enough of
-    // them to keep every SM's copy pipeline busy: the bulk (TMA) family.
-    // Otherwise a block per row, or the two-pass kernel for very wide rows.
+    // Chosen from measurements on B200 (back-to-back calls on cold data):
+    //   rows <= 4 KiB          one block per row, one pack per thread (within
+    //                          0.1-0.2 us of a same-size copy at <= 256 rows)
+    //   4-16 KiB, many rows    one block per row, four packs per thread, a
+    //                          block per row (>= the copy peak at 65536 rows)
+    //   4-16 KiB otherwise     persistent blocks, two packs per thread
+    //   16-32 KiB              rows staged through shared memory (bulk)
+    //   wider                  two-pass block per row
     DeviceInfo dev;
     int rc = current_device_info(&dev);
     if (rc != SM120N_OK) return rc;
-    if (packs <= 4 * kWarpSize) {
-      family = Family::kWarp;
-    } else if (a.rows >= 2 * static_cast<int64_t>(dev.sm_count)) {
+    many_rows = a.rows >= 8 * static_cast<int64_t>(dev.sm_count);
+    if (packs <= 256) {
+      family = a.rows >= 1024 ? Family::kCta : Family::kCtaOnePack;
+    } else if (packs <= 1024) {
+      family = Family::kCta;
+    } else if (packs <= 2048) {
       family = Family::kBulk;
     } else {
-      family = packs <= 1024 ? Family::kCta : Family::kWide;
+      family = Family::kWide;
     }
   }
   if (family == Family::kWarp && packs > 8 * kWarpSize) family = Family::kCta;
@@ -497,10 +517,12 @@ int run_rows(const RowArgs<T>& a, Family family, cudaStream_t stream) {
     case Family::kCtaOnePack:
       return launch_cta<T, kAdd, 1, 1024>(a, round_up_warps(packs), stream);
     case Family::kCta: {
-      // Two packs per thread up to 512 threads keeps 32+ bytes of loads in
-      // flight per thread with a modest register budget.
-      if (packs <= 2 * 512) return launch_cta<T, kAdd, 2, 512>(a, round_up_warps((packs + 1) / 2), stream);
-      return launch_cta<T, kAdd, 4, 256>(a, round_up_warps((packs + 3) / 4), stream);
+      if (many_rows && packs >= 512) {
+        return launch_cta<T, kAdd, 4, 256>(a, round_up_warps((packs + 3) / 4), stream, true);
+      }
+      // Two packs per thread: 32+ bytes of loads in flight per thread with a
+      // modest register budget.
+      return launch_cta<T, kAdd, 2, 512>(a, round_up_warps((packs + 1) / 2), stream);
     }
     case Family::kBulk: {
       size_t block_smem = 0;
