@@ -9,16 +9,19 @@ flushed (a 512 MiB write) before every timed step, outside the timed events.
 ``value`` = algorithmic bytes of all ranks' steps / max-over-ranks device time.
 
 Also reported on the same line:
-  * ``roofline`` -- the dominant kernel of the step (largest total time), its
-    algorithmic bytes per launch over its mean CUDA-event launch duration
-    (each launch after an L2 flush), against the measured HBM copy peak;
+  * ``roofline`` -- the dominant kernel of the step (the longest call), its
+    algorithmic bytes per launch over its launch duration, against the
+    measured HBM copy peak. Launch durations (``per_shape``) come from CUDA
+    events around a graph of R back-to-back calls of one shape on R distinct
+    buffer sets (every call reads data that is not in L2), replayed after an
+    L2 flush: duration = replay time / R;
   * ``e2e`` -- the same sweep through the public API with the inputs copied
     from pinned host memory and both outputs copied back inside the timed
     region;
   * ``per_op`` -- us/call and GB/s of every operator at the other workload
     shapes (batch-1 and wide-batch decode Q/K norm + RoPE + KV store, the
     prefill fused add [65536, 8192] and Q/K prefill of 32768 tokens, and the
-    fp32 RMSNorm rows), each launch after an L2 flush;
+    fp32 RMSNorm rows), timed the same way as ``per_shape``;
   * ``cpu_baseline`` -- the C oracle on the host cores (rank 0, N=1 only).
 
 ``--impl reference`` times the reference path's CPU implementation (the C
@@ -32,7 +35,6 @@ from __future__ import annotations
 
 import argparse
 import json
-import math
 import os
 import statistics
 import subprocess
@@ -339,8 +341,8 @@ def _measure_rest(args, dist, ops, flush, data, step_ms, launches_per_step) -> d
     peak, peak_source = measured_hbm_peak()
     traffic = dram_traffic_per_launch()
     traffic_value = None
-    if traffic and traffic.get("config") == f"fused_add_rms_norm_inplace {dominant['dtype']} " \
-                                            f"{dominant['tokens']}x{dominant['hidden']}":
+    if traffic and traffic.get("config") == \
+            f"fused_add_rms_norm_inplace {dominant['tokens']}x{dominant['hidden']}":
         traffic_value = int(float(traffic.get("dram_bytes_per_launch", "nan")))
     roofline = {"bound": "hbm", "achieved": dominant["gbs"], "peak": peak, "unit": "GB/s",
                 "frac": round(dominant["gbs"] / peak, 4), "traffic": traffic_value,
