@@ -381,7 +381,8 @@ def _measure_rest(args, dist, ops, flush, data, step_ms, launches_per_step) -> d
     b.synchronize()
     e2e_ms = dist.max(a.elapsed_time(b) / e2e_steps)
     e2e = {"value": round(data.bytes * dist.world / (e2e_ms * 1e-3) / 1e9, 2), "unit": "GB/s",
-           "ms_per_step": round(e2e_ms, 4), "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": h2d,
+           "ms_per_step": round(e2e_ms, 4), "h2d_bytes_per_step": h2d * dist.world,
+           "d2h_bytes_per_step": h2d * dist.world,
            "path": "sm120_rmsnorm.fused_add_rms_norm_inplace with pinned-host copies"}
 
     per_op = {} if args.skip_per_op else per_op_suite(ops, flush, dist, args)
