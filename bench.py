@@ -270,56 +270,10 @@ class SweepData:
             ops.fused_add_rms_norm_inplace(x, r, w, EPS)
 
 
-def gpu_arm(args, dist: Dist) -> dict:
-    import sm120_rmsnorm as ops
-
-    dev = torch.device("cuda", torch.cuda.current_device())
-    flush = Flusher()
-    data = SweepData(seed=1234 + dist.rank)
-
-    # CUDA graph of one step (48 launches)
-    for _ in range(3):
-        data.run(ops)
-    torch.cuda.synchronize()
-    graph = torch.cuda.CUDAGraph()
-    with torch.cuda.graph(graph):
-        data.run(ops)
-    launches_per_step = len(data.items)
-
-    for _ in range(args.warmup):
-        flush()
-        graph.replay()
-    dist.barrier()
-    starts, ends = [], []
-    clocks = ClockSampler(sampled_gpus(dist.world) if dist.rank == 0 else None)
-    clocks.__enter__()
-    try:
-        dist.barrier()
-        for _ in range(args.steps):
-            flush()
-            a, b = event_pair()
-            a.record()
-            graph.replay()
-            b.record()
-            starts.append(a)
-            ends.append(b)
-        dist.barrier()
-        step_ms = sum(a.elapsed_time(b) for a, b in zip(starts, ends)) / args.steps
-        line = _measure_rest(args, dist, ops, flush, data, step_ms, launches_per_step)
-    finally:
-        clocks.__exit__(None, None, None)
-    line["clocks"] = clocks.summary() if dist.rank == 0 else None
-    return line
-
-
-def _measure_rest(args, dist, ops, flush, data, step_ms, launches_per_step) -> dict:
-    dev = torch.device("cuda", torch.cuda.current_device())
-    step_ms_max = dist.max(step_ms)
-    value = data.bytes * dist.world / (step_ms_max * 1e-3) / 1e9
-
-    # per-launch durations: for each shape a graph of R back-to-back calls on
-    # R distinct buffer sets (every call reads data that is not in L2),
-    # replayed after an L2 flush; duration = replay time / R
+def per_shape_times(ops, data: "SweepData", flush: "Flusher", dist: "Dist", args) -> list:
+    """Per-launch duration of every sweep shape: a graph of R back-to-back calls
+    on R distinct buffer sets (every call reads data that is not in L2),
+    replayed after an L2 flush; duration = replay time / R."""
     per_shape = []
     g = torch.Generator(device="cuda").manual_seed(77 + dist.rank)
     for t, h, name, x, r, w in data.items:
@@ -335,6 +289,57 @@ def _measure_rest(args, dist, ops, flush, data, step_ms, launches_per_step) -> d
         del shape_graph, bufs, calls
         per_shape.append({"tokens": t, "hidden": h, "dtype": name, "us": round(dist.max(us), 3),
                           "bytes": nbytes, "calls_per_graph": sets})
+    for p in per_shape:
+        p["gbs"] = round(p["bytes"] / (p["us"] * 1e-6) / 1e9, 1)
+    return per_shape
+
+
+def sweep_step_ms(ops, data: "SweepData", flush: "Flusher", steps: int, warmup: int,
+                  dist: "Dist") -> float:
+    """Mean device time of one step (the 48-call sweep as one CUDA graph), L2
+    flushed before every step outside the timed events."""
+    graph, _ = capture([lambda: data.run(ops)])
+    for _ in range(warmup):
+        flush()
+        graph.replay()
+    dist.barrier()
+    pairs = []
+    for _ in range(steps):
+        flush()
+        a, b = event_pair()
+        a.record()
+        graph.replay()
+        b.record()
+        pairs.append((a, b))
+    dist.barrier()
+    return sum(a.elapsed_time(b) for a, b in pairs) / steps
+
+
+def gpu_arm(args, dist: Dist) -> dict:
+    import sm120_rmsnorm as ops
+
+    dev = torch.device("cuda", torch.cuda.current_device())
+    flush = Flusher()
+    data = SweepData(seed=1234 + dist.rank)
+
+    launches_per_step = len(data.items)
+    clocks = ClockSampler(sampled_gpus(dist.world) if dist.rank == 0 else None)
+    clocks.__enter__()
+    try:
+        step_ms = sweep_step_ms(ops, data, flush, args.steps, args.warmup, dist)
+        line = _measure_rest(args, dist, ops, flush, data, step_ms, launches_per_step)
+    finally:
+        clocks.__exit__(None, None, None)
+    line["clocks"] = clocks.summary() if dist.rank == 0 else None
+    return line
+
+
+def _measure_rest(args, dist, ops, flush, data, step_ms, launches_per_step) -> dict:
+    dev = torch.device("cuda", torch.cuda.current_device())
+    step_ms_max = dist.max(step_ms)
+    value = data.bytes * dist.world / (step_ms_max * 1e-3) / 1e9
+
+    per_shape = per_shape_times(ops, data, flush, dist, args)
     for p in per_shape:
         p["gbs"] = round(p["bytes"] / (p["us"] * 1e-6) / 1e9, 1)
     dominant = max(per_shape, key=lambda p: p["us"])
@@ -526,6 +531,49 @@ def cpu_sweep_gbs(seconds: float, threads: int, passes: int | None = None):
     return total * done / elapsed / 1e9, done, elapsed
 
 
+class ReferenceKernels:
+    """The reference project's own CUDA kernels (compiled for sm_100a from its
+    sources by oracle/build_ref.py), called with its ops.py default versions."""
+
+    def __init__(self, module):
+        self.m = module
+
+    def fused_add_rms_norm_inplace(self, x, r, w, eps=EPS, version=0):
+        self.m.fused_add_rms_norm_inplace(x, r, w, eps, version)
+
+    def rms_norm_out(self, x, w, out, eps=EPS, version=2):
+        self.m.rms_norm_out(x, w, out, eps, version)
+
+    def fused_qk_rms_norm_rope_kv(self, q, k, v, qw, kw, pos, cache, kc, vc, slots, eps=EPS,
+                                  version=1):
+        self.m.fused_qk_rms_norm_rope_kv(q, k, v, qw, kw, pos, cache, kc, vc, slots, eps, version)
+
+
+def reference_kernels_gpu(args, dist: Dist) -> dict:
+    """The reference's CUDA kernels on this B200, same workload and timing as
+    the main arm (the SM120 kernels rebuilt for sm_100a: the bar to beat)."""
+    if not torch.cuda.is_available():
+        return {"unavailable": "no CUDA device"}
+    from oracle import build_ref
+
+    module = build_ref.load()
+    if module is None:
+        return {"unavailable": "the reference's kernels were not built (oracle/build_ref.py "
+                               "needs the reference checkout)"}
+    torch.cuda.set_device(0)
+    ops = ReferenceKernels(module)
+    flush = Flusher()
+    data = SweepData(seed=1234)
+    step_ms = sweep_step_ms(ops, data, flush, args.steps, args.warmup, dist)
+    per_shape = per_shape_times(ops, data, flush, dist, args)
+    per_op = {} if args.skip_per_op else per_op_suite(ops, flush, dist, args)
+    return {"value": round(data.bytes / (step_ms * 1e-3) / 1e9, 2), "unit": "GB/s",
+            "ms_per_step": round(step_ms, 5),
+            "build": "reference csrc/rmsnorm_kernels.cu + bindings.cpp, nvcc -O3 "
+                     "--use_fast_math -gencode arch=compute_100a,code=sm_100a",
+            "per_shape": per_shape, "per_op": per_op}
+
+
 def reference_arm(args, dist: Dist) -> dict:
     """The reference path's CPU implementation (C restatement of its PyTorch
     oracle) on the host cores, on the same sweep; rank 0 only."""
@@ -556,6 +604,7 @@ def reference_arm(args, dist: Dist) -> dict:
         "note": "the reference's CPU path is its PyTorch oracle (sm120_rmsnorm/reference.py), "
                 "which cannot travel; this is its C restatement (oracle/norm_oracle.c), "
                 "pinned to the reference's own outputs by the golden-vector tests",
+        "reference_kernels_b200": reference_kernels_gpu(args, dist),
     }
 
 
