@@ -210,6 +210,18 @@ __device__ __forceinline__ void load8_f32(const float* p, float* f) {
   }
 }
 
+// One head of one token, between issuing its loads and finishing it.
+template <typename T>
+struct HeadJob {
+  T* head;
+  Half8<T> x_lo, x_hi, v_lo, v_hi;
+  int64_t position;
+  int64_t slot;
+  int kv_head;
+  bool is_query;
+  bool active;
+};
+
 template <typename T, bool kStoreKV, bool kVector>
 __global__ void __launch_bounds__(256, sizeof(T) == 2 ? 4 : 2) head_norm_rope_kernel(HeadArgs<T> a) {
   wait_for_upstream_grid();
@@ -231,50 +243,54 @@ __global__ void __launch_bounds__(256, sizeof(T) == 2 ? 4 : 2) head_norm_rope_ke
   const Half8<T> kw_lo = load_half<T, kVector>(a.key_weight + lo);
   const Half8<T> kw_hi = load_half<T, kVector>(a.key_weight + hi);
 
-  for (uint32_t first = warp * kHeadsPerWarp; first < units; first += warps * kHeadsPerWarp) {
-    const uint32_t unit = first + head_in_warp;
-    const bool active = unit < units;
-    const uint32_t token = active ? unit / heads : 0;
-    const int h = active ? static_cast<int>(unit - token * heads) : 0;
-    const bool is_query = h < a.query_heads;
-    const int kv_head = h - a.query_heads;
-    T* head = is_query ? a.query + (static_cast<int64_t>(token) * a.query_heads + h) * kHeadDim
-                       : a.key + (static_cast<int64_t>(token) * a.key_heads + kv_head) * kHeadDim;
-
-    Half8<T> x_lo{}, x_hi{}, v_lo, v_hi;
-    int64_t position = -1;
-    int64_t slot = -1;
-    if (active) {
-      x_lo = load_half<T, kVector>(head + lo);
-      x_hi = load_half<T, kVector>(head + hi);
-      position = a.positions[token];
+  auto begin = [&](HeadJob<T>& job, uint32_t unit) {
+    job.active = unit < units;
+    const uint32_t token = job.active ? unit / heads : 0;
+    const int h = job.active ? static_cast<int>(unit - token * heads) : 0;
+    job.is_query = h < a.query_heads;
+    job.kv_head = h - a.query_heads;
+    job.head = job.is_query
+                   ? a.query + (static_cast<int64_t>(token) * a.query_heads + h) * kHeadDim
+                   : a.key + (static_cast<int64_t>(token) * a.key_heads + job.kv_head) * kHeadDim;
+    job.position = -1;
+    job.slot = -1;
+    job.x_lo = Half8<T>{};
+    job.x_hi = Half8<T>{};
+    if (job.active) {
+      job.x_lo = load_half<T, kVector>(job.head + lo);
+      job.x_hi = load_half<T, kVector>(job.head + hi);
+      job.position = a.positions[token];
       if constexpr (kStoreKV) {
-        if (!is_query) {
-          slot = a.slots[token];
-          if (slot >= 0 && slot < a.cache_slots) {
-            const T* vh = a.value + (static_cast<int64_t>(token) * a.key_heads + kv_head) * kHeadDim;
-            v_lo = load_half<T, kVector>(vh + lo);
-            v_hi = load_half<T, kVector>(vh + hi);
+        if (!job.is_query) {
+          job.slot = a.slots[token];
+          if (job.slot >= 0 && job.slot < a.cache_slots) {
+            const T* vh =
+                a.value + (static_cast<int64_t>(token) * a.key_heads + job.kv_head) * kHeadDim;
+            job.v_lo = load_half<T, kVector>(vh + lo);
+            job.v_hi = load_half<T, kVector>(vh + hi);
           } else {
-            slot = -1;
+            job.slot = -1;
           }
         }
       }
     }
+  };
 
-    float sum_sq = half_sum_squares<T>(x_hi, half_sum_squares<T>(x_lo, 0.0f));
-    sum_sq = group_allreduce_sum<kLanesPerHead>(sum_sq);
-    if (!active || position < 0 || position >= a.rope_positions) continue;
+  auto finish = [&](const HeadJob<T>& job) {
+    float sum_sq = half_sum_squares<T>(job.x_hi, half_sum_squares<T>(job.x_lo, 0.0f));
+    sum_sq = group_allreduce_sum<kLanesPerHead>(sum_sq);  // all lanes, before any exit
+    if (!job.active || job.position < 0 || job.position >= a.rope_positions) return;
     // mean over 128 elements: a multiply by an exact power of two
     const float inv = __fdiv_rn(
         1.0f, __fsqrt_rn(__fadd_rn(__fmul_rn(sum_sq, 1.0f / kHeadDim), a.epsilon)));
-
-    const Half8<T> n_lo = normalise_half<T>(x_lo, select_half<T>(is_query, qw_lo, kw_lo), inv);
-    const Half8<T> n_hi = normalise_half<T>(x_hi, select_half<T>(is_query, qw_hi, kw_hi), inv);
+    const Half8<T> n_lo =
+        normalise_half<T>(job.x_lo, select_half<T>(job.is_query, qw_lo, kw_lo), inv);
+    const Half8<T> n_hi =
+        normalise_half<T>(job.x_hi, select_half<T>(job.is_query, qw_hi, kw_hi), inv);
 
     float c[kElemsPerHalf], s[kElemsPerHalf], p[kElemsPerHalf], q[kElemsPerHalf];
-    load8_f32<kVector>(a.cos_sin + position * kHeadDim + lo, c);
-    load8_f32<kVector>(a.cos_sin + position * kHeadDim + hi, s);
+    load8_f32<kVector>(a.cos_sin + job.position * kHeadDim + lo, c);
+    load8_f32<kVector>(a.cos_sin + job.position * kHeadDim + hi, s);
     unpack_half<T>(n_lo, p);
     unpack_half<T>(n_hi, q);
     float y_lo[kElemsPerHalf], y_hi[kElemsPerHalf];
@@ -285,17 +301,23 @@ __global__ void __launch_bounds__(256, sizeof(T) == 2 ? 4 : 2) head_norm_rope_ke
     }
     const Half8<T> out_lo = pack_half<T>(y_lo);
     const Half8<T> out_hi = pack_half<T>(y_hi);
-    store_half<T, kVector>(head + lo, out_lo);
-    store_half<T, kVector>(head + hi, out_hi);
+    store_half<T, kVector>(job.head + lo, out_lo);
+    store_half<T, kVector>(job.head + hi, out_hi);
     if constexpr (kStoreKV) {
-      if (slot >= 0) {
-        const int64_t cache_head = (slot * a.key_heads + kv_head) * kHeadDim;
+      if (job.slot >= 0) {
+        const int64_t cache_head = (job.slot * a.key_heads + job.kv_head) * kHeadDim;
         store_half<T, kVector>(a.key_cache + cache_head + lo, out_lo);  // same bits as K
         store_half<T, kVector>(a.key_cache + cache_head + hi, out_hi);
-        store_half<T, kVector>(a.value_cache + cache_head + lo, v_lo);
-        store_half<T, kVector>(a.value_cache + cache_head + hi, v_hi);
+        store_half<T, kVector>(a.value_cache + cache_head + lo, job.v_lo);
+        store_half<T, kVector>(a.value_cache + cache_head + hi, job.v_hi);
       }
     }
+  };
+
+  for (uint32_t first = warp * kHeadsPerWarp; first < units; first += warps * kHeadsPerWarp) {
+    HeadJob<T> job;
+    begin(job, first + head_in_warp);
+    finish(job);
   }
 }
 
@@ -313,6 +335,7 @@ int run_heads(HeadArgs<T> a, int threads_per_block, cudaStream_t stream) {
   if (rc != SM120N_OK) return rc;
   auto kernel = vector ? head_norm_rope_kernel<T, kStoreKV, true>
                        : head_norm_rope_kernel<T, kStoreKV, false>;
+  const int64_t heads_per_warp = kHeadsPerWarp;
   // Keep tokens * heads below 2^31 per launch (the kernel indexes units in
   // 32 bits); larger calls become consecutive launches on the same stream.
   const int64_t max_tokens = ((int64_t{1} << 31) - 1) / heads;
@@ -328,7 +351,7 @@ int run_heads(HeadArgs<T> a, int threads_per_block, cudaStream_t stream) {
       c.slots = a.slots + done;
     }
     const int64_t units = c.tokens * heads;
-    const int64_t warps_needed = (units + kHeadsPerWarp - 1) / kHeadsPerWarp;
+    const int64_t warps_needed = (units + heads_per_warp - 1) / heads_per_warp;
     int64_t threads = threads_per_block;
     int64_t blocks;
     if (threads == 0) {
