@@ -93,6 +93,41 @@ struct Pack<__half> {
   }
 };
 
+// A pack as element pairs (2i, 2i+1), the operand shape of the sm_100 packed
+// fp32x2 instructions (__fadd2_rn / __fmul2_rn / __ffma2_rn: two IEEE
+// round-to-nearest-even operations per instruction, each identical to the
+// scalar one).
+template <typename T>
+__device__ __forceinline__ void pack_to_pairs(const uint4& p, float2* f) {
+  float g[Pack<T>::kElems];
+  Pack<T>::to_f32(p, g);
+#pragma unroll
+  for (int i = 0; i < Pack<T>::kElems / 2; ++i) f[i] = make_float2(g[2 * i], g[2 * i + 1]);
+}
+
+template <typename T>
+__device__ __forceinline__ uint4 pairs_to_pack(const float2* f) {
+  float g[Pack<T>::kElems];
+#pragma unroll
+  for (int i = 0; i < Pack<T>::kElems / 2; ++i) {
+    g[2 * i] = f[i].x;
+    g[2 * i + 1] = f[i].y;
+  }
+  return Pack<T>::from_f32(g);
+}
+
+// Adds the squares of n pairs to a pair of accumulators. For 16-bit storage
+// types x^2 is exact in fp32, so an FMA equals a rounded square followed by a
+// rounded add; fp32 inputs take the separate multiply.
+template <typename T>
+__device__ __forceinline__ float2 accumulate_square_pairs(float2 acc, const float2* f, int n) {
+#pragma unroll
+  for (int i = 0; i < n; ++i) {
+    acc = sizeof(T) == 2 ? __ffma2_rn(f[i], f[i], acc) : __fadd2_rn(acc, __fmul2_rn(f[i], f[i]));
+  }
+  return acc;
+}
+
 // Scalar element access for the unaligned fallback kernels.
 template <typename T>
 struct Scalar;

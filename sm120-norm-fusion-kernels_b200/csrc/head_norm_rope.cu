@@ -56,7 +56,34 @@ struct HeadArgs {
   int64_t rope_positions;
   int64_t cache_slots;
   float epsilon;
+  // unit -> token division by heads = query_heads + key_heads, for unit
+  // indices below 2^31: q = heads_pow2 ? u >> heads_shift
+  //                                    : umulhi(u, heads_magic) >> (heads_shift - 1)
+  uint32_t heads_magic;
+  int heads_shift;
+  bool heads_pow2;
 };
+
+// Constants for dividing indices below 2^31 by d (1 <= d <= 2^20): with
+// l = ceil(log2 d), m = ceil(2^(31+l) / d) satisfies 2^(31+l) <= m*d <=
+// 2^(31+l) + 2^l, so floor(n*m / 2^(31+l)) = floor(n / d) (the round-up
+// method for division by invariant integers).
+template <typename T>
+void set_head_divisor(HeadArgs<T>& a) {
+  const uint32_t d = static_cast<uint32_t>(a.query_heads + a.key_heads);
+  int l = 0;
+  while ((uint64_t{1} << l) < d) ++l;
+  a.heads_shift = l;
+  a.heads_pow2 = (d & (d - 1)) == 0;
+  a.heads_magic = a.heads_pow2 ? 0u
+                               : static_cast<uint32_t>(((uint64_t{1} << (31 + l)) + d - 1) / d);
+}
+
+template <typename T>
+__device__ __forceinline__ uint32_t token_of_unit(const HeadArgs<T>& a, uint32_t unit) {
+  return a.heads_pow2 ? unit >> a.heads_shift
+                      : __umulhi(unit, a.heads_magic) >> (a.heads_shift - 1);
+}
 
 // Eight elements of T as 32-bit words: four words (two elements each) for
 // 16-bit types, eight for fp32. Loaded with 16-byte accesses when the buffers
@@ -111,27 +138,30 @@ __device__ __forceinline__ void store_half(T* p, const Half8<T>& h) {
   }
 }
 
-// Element e of a half as fp32.
+// Elements (2i, 2i+1) of a half as float2 number i.
 template <typename T>
-__device__ __forceinline__ void unpack_half(const Half8<T>& h, float* f) {
-  if constexpr (sizeof(T) == 4) {
+__device__ __forceinline__ void unpack_pairs(const Half8<T>& h, float2* f) {
 #pragma unroll
-    for (int i = 0; i < 8; ++i) f[i] = __uint_as_float(h.w[i]);
-  } else {
-#pragma unroll
-    for (int i = 0; i < 4; ++i) Pack<T>::word_to_f32(h.w[i], f[2 * i], f[2 * i + 1]);
+  for (int i = 0; i < 4; ++i) {
+    if constexpr (sizeof(T) == 4) {
+      f[i] = make_float2(__uint_as_float(h.w[2 * i]), __uint_as_float(h.w[2 * i + 1]));
+    } else {
+      Pack<T>::word_to_f32(h.w[i], f[i].x, f[i].y);
+    }
   }
 }
 
 template <typename T>
-__device__ __forceinline__ Half8<T> pack_half(const float* f) {
+__device__ __forceinline__ Half8<T> pack_pairs(const float2* f) {
   Half8<T> h;
-  if constexpr (sizeof(T) == 4) {
 #pragma unroll
-    for (int i = 0; i < 8; ++i) h.w[i] = __float_as_uint(f[i]);
-  } else {
-#pragma unroll
-    for (int i = 0; i < 4; ++i) h.w[i] = Pack<T>::f32_to_word(f[2 * i], f[2 * i + 1]);
+  for (int i = 0; i < 4; ++i) {
+    if constexpr (sizeof(T) == 4) {
+      h.w[2 * i] = __float_as_uint(f[i].x);
+      h.w[2 * i + 1] = __float_as_uint(f[i].y);
+    } else {
+      h.w[i] = Pack<T>::f32_to_word(f[i].x, f[i].y);
+    }
   }
   return h;
 }
@@ -153,15 +183,17 @@ __device__ __forceinline__ uint32_t mul_pair_rn<__half>(uint32_t a, uint32_t b) 
   return *reinterpret_cast<uint32_t*>(&r);
 }
 
-// Sum of the squares of a half. For 16-bit types x^2 is exact in fp32, so an
-// FMA equals the oracle's rounded square followed by a rounded add.
+// Sum of squares of a half into a pair of accumulators (even / odd
+// elements), with the sm_100 packed fp32x2 instructions. For 16-bit types x^2
+// is exact in fp32, so the FMA equals the oracle's rounded square followed by
+// a rounded add.
 template <typename T>
-__device__ __forceinline__ float half_sum_squares(const Half8<T>& h, float acc) {
-  float f[kElemsPerHalf];
-  unpack_half<T>(h, f);
+__device__ __forceinline__ float2 half_sum_squares(const Half8<T>& h, float2 acc) {
+  float2 f[4];
+  unpack_pairs<T>(h, f);
 #pragma unroll
-  for (int i = 0; i < kElemsPerHalf; ++i) {
-    acc = sizeof(T) == 2 ? __fmaf_rn(f[i], f[i], acc) : __fadd_rn(acc, __fmul_rn(f[i], f[i]));
+  for (int i = 0; i < 4; ++i) {
+    acc = sizeof(T) == 2 ? __ffma2_rn(f[i], f[i], acc) : __fadd2_rn(acc, __fmul2_rn(f[i], f[i]));
   }
   return acc;
 }
@@ -171,22 +203,53 @@ __device__ __forceinline__ float half_sum_squares(const Half8<T>& h, float acc) 
 template <typename T>
 __device__ __forceinline__ Half8<T> normalise_half(const Half8<T>& x, const Half8<T>& w,
                                                    float inv) {
-  Half8<T> n;
+  const float2 inv2 = make_float2(inv, inv);
+  float2 f[4];
+  unpack_pairs<T>(x, f);
   if constexpr (sizeof(T) == 4) {
+    float2 g[4];
+    unpack_pairs<T>(w, g);
 #pragma unroll
-    for (int i = 0; i < 8; ++i) {
-      n.w[i] = __float_as_uint(
-          __fmul_rn(__fmul_rn(__uint_as_float(x.w[i]), inv), __uint_as_float(w.w[i])));
-    }
+    for (int i = 0; i < 4; ++i) f[i] = __fmul2_rn(__fmul2_rn(f[i], inv2), g[i]);
+    return pack_pairs<T>(f);
   } else {
+    Half8<T> n;
 #pragma unroll
     for (int i = 0; i < 4; ++i) {
-      float a, b;
-      Pack<T>::word_to_f32(x.w[i], a, b);
-      n.w[i] = mul_pair_rn<T>(Pack<T>::f32_to_word(__fmul_rn(a, inv), __fmul_rn(b, inv)), w.w[i]);
+      const float2 t = __fmul2_rn(f[i], inv2);
+      n.w[i] = mul_pair_rn<T>(Pack<T>::f32_to_word(t.x, t.y), w.w[i]);
     }
+    return n;
   }
-  return n;
+}
+
+// Half-split rotation of one lane's pairs: lo = n_lo*c - n_hi*s,
+// hi = n_hi*c + n_lo*s, each product and sum rounded on its own (the
+// subtraction is an add of the negated product, exact under round to nearest
+// even).
+template <typename T>
+__device__ __forceinline__ void rotate_half(const Half8<T>& n_lo, const Half8<T>& n_hi,
+                                            const float2* c, const float2* s,
+                                            Half8<T>& out_lo, Half8<T>& out_hi) {
+  float2 p[4], q[4], y_lo[4], y_hi[4];
+  unpack_pairs<T>(n_lo, p);
+  unpack_pairs<T>(n_hi, q);
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const float2 qs = __fmul2_rn(q[i], s[i]);
+    y_lo[i] = __fadd2_rn(__fmul2_rn(p[i], c[i]), make_float2(-qs.x, -qs.y));
+    y_hi[i] = __fadd2_rn(__fmul2_rn(q[i], c[i]), __fmul2_rn(p[i], s[i]));
+  }
+  out_lo = pack_pairs<T>(y_lo);
+  out_hi = pack_pairs<T>(y_hi);
+}
+
+// 1 / sqrt(sum_sq / 128 + eps): the mean is a multiply by an exact power of
+// two; the reciprocal is correctly rounded, as a correctly rounded divide of
+// 1 would be.
+__device__ __forceinline__ float head_inverse_rms(float2 acc, float eps) {
+  const float sum = __fadd_rn(acc.x, acc.y);
+  return __frcp_rn(__fsqrt_rn(__fadd_rn(__fmul_rn(sum, 1.0f / kHeadDim), eps)));
 }
 
 template <typename T>
@@ -197,16 +260,19 @@ __device__ __forceinline__ Half8<T> select_half(bool first, const Half8<T>& a, c
   return r;
 }
 
+// Eight consecutive fp32 values (cos or sin) as four pairs.
 template <bool kVector>
-__device__ __forceinline__ void load8_f32(const float* p, float* f) {
+__device__ __forceinline__ void load8_pairs(const float* p, float2* f) {
   if constexpr (kVector) {
     const float4 a = *reinterpret_cast<const float4*>(p);
     const float4 b = *reinterpret_cast<const float4*>(p + 4);
-    f[0] = a.x; f[1] = a.y; f[2] = a.z; f[3] = a.w;
-    f[4] = b.x; f[5] = b.y; f[6] = b.z; f[7] = b.w;
+    f[0] = make_float2(a.x, a.y);
+    f[1] = make_float2(a.z, a.w);
+    f[2] = make_float2(b.x, b.y);
+    f[3] = make_float2(b.z, b.w);
   } else {
 #pragma unroll
-    for (int i = 0; i < 8; ++i) f[i] = p[i];
+    for (int i = 0; i < 4; ++i) f[i] = make_float2(p[2 * i], p[2 * i + 1]);
   }
 }
 
@@ -245,7 +311,7 @@ __global__ void __launch_bounds__(256, sizeof(T) == 2 ? 4 : 2) head_norm_rope_ke
 
   auto begin = [&](HeadJob<T>& job, uint32_t unit) {
     job.active = unit < units;
-    const uint32_t token = job.active ? unit / heads : 0;
+    const uint32_t token = job.active ? token_of_unit(a, unit) : 0;
     const int h = job.active ? static_cast<int>(unit - token * heads) : 0;
     job.is_query = h < a.query_heads;
     job.kv_head = h - a.query_heads;
@@ -277,30 +343,20 @@ __global__ void __launch_bounds__(256, sizeof(T) == 2 ? 4 : 2) head_norm_rope_ke
   };
 
   auto finish = [&](const HeadJob<T>& job) {
-    float sum_sq = half_sum_squares<T>(job.x_hi, half_sum_squares<T>(job.x_lo, 0.0f));
-    sum_sq = group_allreduce_sum<kLanesPerHead>(sum_sq);  // all lanes, before any exit
+    float2 acc = half_sum_squares<T>(job.x_hi, half_sum_squares<T>(job.x_lo, make_float2(0.f, 0.f)));
+    const float lane_sum = __fadd_rn(acc.x, acc.y);
+    const float total = group_allreduce_sum<kLanesPerHead>(lane_sum);  // all lanes, before any exit
     if (!job.active || job.position < 0 || job.position >= a.rope_positions) return;
-    // mean over 128 elements: a multiply by an exact power of two
-    const float inv = __fdiv_rn(
-        1.0f, __fsqrt_rn(__fadd_rn(__fmul_rn(sum_sq, 1.0f / kHeadDim), a.epsilon)));
+    const float inv = head_inverse_rms(make_float2(total, 0.0f), a.epsilon);
     const Half8<T> n_lo =
         normalise_half<T>(job.x_lo, select_half<T>(job.is_query, qw_lo, kw_lo), inv);
     const Half8<T> n_hi =
         normalise_half<T>(job.x_hi, select_half<T>(job.is_query, qw_hi, kw_hi), inv);
-
-    float c[kElemsPerHalf], s[kElemsPerHalf], p[kElemsPerHalf], q[kElemsPerHalf];
-    load8_f32<kVector>(a.cos_sin + job.position * kHeadDim + lo, c);
-    load8_f32<kVector>(a.cos_sin + job.position * kHeadDim + hi, s);
-    unpack_half<T>(n_lo, p);
-    unpack_half<T>(n_hi, q);
-    float y_lo[kElemsPerHalf], y_hi[kElemsPerHalf];
-#pragma unroll
-    for (int i = 0; i < kElemsPerHalf; ++i) {
-      y_lo[i] = __fsub_rn(__fmul_rn(p[i], c[i]), __fmul_rn(q[i], s[i]));
-      y_hi[i] = __fadd_rn(__fmul_rn(q[i], c[i]), __fmul_rn(p[i], s[i]));
-    }
-    const Half8<T> out_lo = pack_half<T>(y_lo);
-    const Half8<T> out_hi = pack_half<T>(y_hi);
+    float2 c[4], sn[4];
+    load8_pairs<kVector>(a.cos_sin + job.position * kHeadDim + lo, c);
+    load8_pairs<kVector>(a.cos_sin + job.position * kHeadDim + hi, sn);
+    Half8<T> out_lo, out_hi;
+    rotate_half<T>(n_lo, n_hi, c, sn, out_lo, out_hi);
     store_half<T, kVector>(job.head + lo, out_lo);
     store_half<T, kVector>(job.head + hi, out_hi);
     if constexpr (kStoreKV) {
@@ -321,6 +377,201 @@ __global__ void __launch_bounds__(256, sizeof(T) == 2 ? 4 : 2) head_norm_rope_ke
   }
 }
 
+// ---- bulk variant: tokens staged through shared memory by the TMA engine ---
+// Persistent blocks; block b owns tokens b, b + gridDim.x, ... and keeps up to
+// `stages` of them in flight. Thread 0 copies a token's Q heads, K heads,
+// V heads (contiguous per token) and its 512-byte cos/sin row into a stage
+// with cp.async.bulk, completion counted by the stage's mbarrier. Positions
+// and slots are prefetched for 256 tokens at a time into shared memory, so the
+// issuing thread never waits on a dependent load. Every lane group processes
+// heads out of the stage and stores results straight from registers; the
+// block barrier that ends a token also proves the stage has been read, and
+// thread 0 then refills it with the token `stages` ahead.
+__device__ unsigned int g_expired_waits_heads = 0;
+
+constexpr int kMaxTokenStages = 8;
+constexpr int kPrefetch = 256;  // tokens per position / slot prefetch (= block size)
+
+template <typename T, bool kStoreKV>
+__global__ void __launch_bounds__(256) head_norm_rope_bulk_kernel(HeadArgs<T> a, int stages) {
+  extern __shared__ __align__(128) unsigned char stage_memory[];
+  __shared__ __align__(8) uint64_t stage_full[kMaxTokenStages];
+  __shared__ int64_t stage_position[kMaxTokenStages];
+  __shared__ int64_t stage_slot[kMaxTokenStages];
+  __shared__ int64_t prefetch_position[2][kPrefetch];
+  __shared__ int32_t prefetch_slot[2][kPrefetch];
+
+  const int lane = threadIdx.x & (kWarpSize - 1);
+  const int part = lane % kLanesPerHead;
+  const int head_in_warp = lane / kLanesPerHead;
+  const int warp = threadIdx.x / kWarpSize;
+  const int warps = blockDim.x / kWarpSize;
+  const int lo = part * kElemsPerHalf;
+  const int hi = kHalf + lo;
+  const int heads = a.query_heads + a.key_heads;
+  constexpr uint32_t kHeadBytes = kHeadDim * sizeof(T);
+  const uint32_t q_bytes = static_cast<uint32_t>(a.query_heads) * kHeadBytes;
+  const uint32_t k_bytes = static_cast<uint32_t>(a.key_heads) * kHeadBytes;
+  const uint32_t v_bytes = kStoreKV ? k_bytes : 0;
+  const uint32_t rope_offset = q_bytes + k_bytes + v_bytes;
+  const uint32_t stage_bytes = rope_offset + kHeadDim * sizeof(float);
+  const int64_t first_token = blockIdx.x;
+  const int64_t my_tokens =
+      first_token < a.tokens ? (a.tokens - first_token + gridDim.x - 1) / gridDim.x : 0;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < stages; ++s) mbarrier_init(&stage_full[s], 1);
+    fence_mbarrier_init();
+  }
+  __syncthreads();
+  wait_for_upstream_grid();
+  release_downstream_grid();
+
+  auto token_of = [&](int64_t j) { return first_token + j * gridDim.x; };
+  auto prefetch = [&](int64_t chunk) {  // every thread: one token of the chunk
+    const int64_t j = chunk * kPrefetch + threadIdx.x;
+    if (threadIdx.x < kPrefetch && j < my_tokens) {
+      const int64_t t = token_of(j);
+      prefetch_position[chunk & 1][threadIdx.x] = a.positions[t];
+      if constexpr (kStoreKV) {  // slot_mapping may be absent when there are no KV heads
+        prefetch_slot[chunk & 1][threadIdx.x] = a.key_heads > 0 ? a.slots[t] : -1;
+      }
+    }
+  };
+  auto fill = [&](int64_t j) {  // thread 0
+    const int s = static_cast<int>(j % stages);
+    const int64_t t = token_of(j);
+    const int64_t position = prefetch_position[(j / kPrefetch) & 1][j % kPrefetch];
+    const int64_t slot = kStoreKV ? prefetch_slot[(j / kPrefetch) & 1][j % kPrefetch] : -1;
+    const bool rope = position >= 0 && position < a.rope_positions;
+    stage_position[s] = position;
+    stage_slot[s] = slot;
+    unsigned char* dst = stage_memory + static_cast<size_t>(s) * stage_bytes;
+    mbarrier_arrive_expect_tx(&stage_full[s],
+                              rope_offset + (rope ? kHeadDim * sizeof(float) : 0));
+    if (q_bytes) bulk_load(dst, a.query + t * a.query_heads * kHeadDim, q_bytes, &stage_full[s]);
+    if (k_bytes) bulk_load(dst + q_bytes, a.key + t * a.key_heads * kHeadDim, k_bytes, &stage_full[s]);
+    if (v_bytes) {
+      bulk_load(dst + q_bytes + k_bytes, a.value + t * a.key_heads * kHeadDim, v_bytes,
+                &stage_full[s]);
+    }
+    if (rope) {
+      bulk_load(dst + rope_offset, a.cos_sin + position * kHeadDim, kHeadDim * sizeof(float),
+                &stage_full[s]);
+    }
+  };
+
+  prefetch(0);
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    for (int64_t j = 0; j < my_tokens && j < stages; ++j) fill(j);
+  }
+  const Half8<T> qw_lo = load_half<T, true>(a.query_weight + lo);
+  const Half8<T> qw_hi = load_half<T, true>(a.query_weight + hi);
+  const Half8<T> kw_lo = load_half<T, true>(a.key_weight + lo);
+  const Half8<T> kw_hi = load_half<T, true>(a.key_weight + hi);
+
+  for (int64_t j = 0; j < my_tokens; ++j) {
+    if (j % kPrefetch == 0 && (j / kPrefetch + 1) * kPrefetch < my_tokens) {
+      prefetch(j / kPrefetch + 1);  // read by thread 0 only after later barriers
+    }
+    const int s = static_cast<int>(j % stages);
+    const bool arrived =
+        mbarrier_wait_bounded(&stage_full[s], static_cast<uint32_t>((j / stages) & 1));
+    const unsigned char* stage = stage_memory + static_cast<size_t>(s) * stage_bytes;
+    const int64_t t = token_of(j);
+    const int64_t position = stage_position[s];
+    const int64_t slot = stage_slot[s];
+    const bool rope = arrived && position >= 0 && position < a.rope_positions;
+    const bool store_kv = kStoreKV && slot >= 0 && slot < a.cache_slots;
+    float2 c[4], sn[4];
+    if (rope) {
+      load8_pairs<true>(reinterpret_cast<const float*>(stage + rope_offset) + lo, c);
+      load8_pairs<true>(reinterpret_cast<const float*>(stage + rope_offset) + hi, sn);
+    }
+    for (int base = warp * kHeadsPerWarp; base < heads; base += warps * kHeadsPerWarp) {
+      const int h = base + head_in_warp;
+      const bool active = h < heads;
+      const bool is_query = h < a.query_heads;
+      const int kv_head = h - a.query_heads;
+      const uint32_t in_stage = is_query ? h * kHeadBytes : q_bytes + kv_head * kHeadBytes;
+      Half8<T> x_lo{}, x_hi{};
+      if (active) {
+        x_lo = load_half<T, true>(reinterpret_cast<const T*>(stage + in_stage) + lo);
+        x_hi = load_half<T, true>(reinterpret_cast<const T*>(stage + in_stage) + hi);
+      }
+      float2 acc = half_sum_squares<T>(x_hi, half_sum_squares<T>(x_lo, make_float2(0.f, 0.f)));
+      const float total = group_allreduce_sum<kLanesPerHead>(__fadd_rn(acc.x, acc.y));  // all lanes
+      if (!active || !rope) continue;
+      const float inv = head_inverse_rms(make_float2(total, 0.0f), a.epsilon);
+      const Half8<T> n_lo = normalise_half<T>(x_lo, select_half<T>(is_query, qw_lo, kw_lo), inv);
+      const Half8<T> n_hi = normalise_half<T>(x_hi, select_half<T>(is_query, qw_hi, kw_hi), inv);
+      Half8<T> out_lo, out_hi;
+      rotate_half<T>(n_lo, n_hi, c, sn, out_lo, out_hi);
+      T* head = is_query ? a.query + (t * a.query_heads + h) * kHeadDim
+                         : a.key + (t * a.key_heads + kv_head) * kHeadDim;
+      store_half<T, true>(head + lo, out_lo);
+      store_half<T, true>(head + hi, out_hi);
+      if constexpr (kStoreKV) {
+        if (!is_query && store_kv) {
+          const int64_t cache_head = (slot * a.key_heads + kv_head) * kHeadDim;
+          const T* v = reinterpret_cast<const T*>(stage + q_bytes + k_bytes + kv_head * kHeadBytes);
+          store_half<T, true>(a.key_cache + cache_head + lo, out_lo);  // same bits as K
+          store_half<T, true>(a.key_cache + cache_head + hi, out_hi);
+          store_half<T, true>(a.value_cache + cache_head + lo, load_half<T, true>(v + lo));
+          store_half<T, true>(a.value_cache + cache_head + hi, load_half<T, true>(v + hi));
+        }
+      }
+    }
+    if (__syncthreads_or(!arrived)) {
+      // A copy never completed within the bound: record it, give copies still
+      // in flight a bounded chance to land, and leave this block's tokens.
+      if (threadIdx.x == 0) {
+        atomicAdd(&g_expired_waits_heads, 1u);
+        for (int64_t i = j; i < my_tokens && i < j + stages; ++i) {
+          mbarrier_wait_bounded(&stage_full[i % stages], static_cast<uint32_t>((i / stages) & 1));
+        }
+      }
+      __syncthreads();
+      return;
+    }
+    if (threadIdx.x == 0 && j + stages < my_tokens) {
+      fence_async_shared();  // this stage's shared-memory reads before the refill
+      fill(j + stages);
+    }
+  }
+}
+
+// Launches the bulk variant when its stages fit; *launched reports whether.
+template <typename T, bool kStoreKV>
+int launch_heads_bulk(const HeadArgs<T>& a, cudaStream_t stream, bool* launched) {
+  *launched = false;
+  const size_t stage_bytes =
+      static_cast<size_t>(a.query_heads + a.key_heads + (kStoreKV ? a.key_heads : 0)) *
+          kHeadDim * sizeof(T) + kHeadDim * sizeof(float);
+  size_t block_smem = 0;
+  int rc = max_block_smem(&block_smem);
+  if (rc != SM120N_OK) return rc;
+  const size_t static_smem = 8 * 1024;  // barriers, per-stage indices, prefetch arrays
+  int stages = static_cast<int>(std::min<size_t>(kMaxTokenStages, (64 * 1024) / stage_bytes));
+  stages = std::max(stages, 2);
+  if (stages * stage_bytes + static_smem > block_smem) return SM120N_OK;
+  const size_t smem = stages * stage_bytes;
+  auto kernel = head_norm_rope_bulk_kernel<T, kStoreKV>;
+  rc = allow_dynamic_smem(reinterpret_cast<const void*>(kernel), smem);
+  if (rc != SM120N_OK) return rc;
+  DeviceInfo dev;
+  rc = current_device_info(&dev);
+  if (rc != SM120N_OK) return rc;
+  int resident = 1;
+  rc = max_resident_ctas(reinterpret_cast<const void*>(kernel), 256, smem, &resident);
+  if (rc != SM120N_OK) return rc;
+  const int64_t grid = std::max<int64_t>(
+      1, std::min<int64_t>(a.tokens, static_cast<int64_t>(dev.sm_count) * resident));
+  *launched = true;
+  return launch(kernel, dim3(static_cast<unsigned>(grid)), dim3(256), smem, stream, a, stages);
+}
+
 // threads_per_block == 0 selects the B200 default: up to 256 threads and a
 // persistent grid capped at what is resident on the device.
 template <typename T, bool kStoreKV>
@@ -333,6 +584,13 @@ int run_heads(HeadArgs<T> a, int threads_per_block, cudaStream_t stream) {
   DeviceInfo dev;
   int rc = current_device_info(&dev);
   if (rc != SM120N_OK) return rc;
+  // Many tokens: stage them through shared memory (bulk copies); the default
+  // launch only, the fixed-shape versions keep the register kernel.
+  if (vector && threads_per_block == 0 && a.tokens >= 2 * static_cast<int64_t>(dev.sm_count)) {
+    bool launched = false;
+    rc = launch_heads_bulk<T, kStoreKV>(a, stream, &launched);
+    if (rc != SM120N_OK || launched) return rc;
+  }
   auto kernel = vector ? head_norm_rope_kernel<T, kStoreKV, true>
                        : head_norm_rope_kernel<T, kStoreKV, false>;
   const int64_t heads_per_warp = kHeadsPerWarp;
@@ -340,6 +598,7 @@ int run_heads(HeadArgs<T> a, int threads_per_block, cudaStream_t stream) {
   // 32 bits); larger calls become consecutive launches on the same stream.
   const int64_t max_tokens = ((int64_t{1} << 31) - 1) / heads;
   const int64_t all_tokens = a.tokens;
+  set_head_divisor(a);
   for (int64_t done = 0; done < all_tokens; done += max_tokens) {
     HeadArgs<T> c = a;
     c.tokens = std::min(max_tokens, all_tokens - done);
@@ -419,6 +678,24 @@ int check_heads(int64_t tokens, int64_t query_heads, int64_t key_heads, int64_t 
 }
 
 }  // namespace
+
+int read_head_faults(unsigned int* out) {
+  const cudaError_t err = cudaMemcpyFromSymbol(out, g_expired_waits_heads, sizeof *out);
+  if (err != cudaSuccess) {
+    return fail(SM120N_ERR_CUDA, "reading the fault counter failed: %s", cudaGetErrorString(err));
+  }
+  return SM120N_OK;
+}
+
+int reset_head_faults() {
+  const unsigned int zero = 0;
+  const cudaError_t err = cudaMemcpyToSymbol(g_expired_waits_heads, &zero, sizeof zero);
+  if (err != cudaSuccess) {
+    return fail(SM120N_ERR_CUDA, "resetting the fault counter failed: %s", cudaGetErrorString(err));
+  }
+  return SM120N_OK;
+}
+
 }  // namespace sm120n
 
 using namespace sm120n;

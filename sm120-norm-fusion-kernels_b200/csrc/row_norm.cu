@@ -51,34 +51,37 @@ struct RowArgs {
   float epsilon;
 };
 
-// s = round(x + r) for one pack (kAdd), returned packed; f receives fp32 s.
+// s = round(x + r) for one pack (kAdd), returned packed; its square is added
+// to `acc` (a pair of accumulators: even and odd elements).
 template <typename T, bool kAdd>
-__device__ __forceinline__ uint4 combine(const uint4& x, const uint4& r, float* f) {
-  using P = Pack<T>;
-  P::to_f32(x, f);
+__device__ __forceinline__ uint4 combine(const uint4& x, const uint4& r, float2& acc) {
+  constexpr int kPairs = Pack<T>::kElems / 2;
+  float2 f[kPairs];
+  pack_to_pairs<T>(x, f);
+  uint4 s = x;
   if constexpr (kAdd) {
-    float g[P::kElems];
-    P::to_f32(r, g);
+    float2 g[kPairs];
+    pack_to_pairs<T>(r, g);
 #pragma unroll
-    for (int e = 0; e < P::kElems; ++e) f[e] = __fadd_rn(f[e], g[e]);
-    const uint4 s = P::from_f32(f);
-    P::to_f32(s, f);  // the rounded sum is what the oracle squares
-    return s;
-  } else {
-    return x;
+    for (int i = 0; i < kPairs; ++i) f[i] = __fadd2_rn(f[i], g[i]);
+    s = pairs_to_pack<T>(f);
+    pack_to_pairs<T>(s, f);  // the rounded sum is what the oracle squares
   }
+  acc = accumulate_square_pairs<T>(acc, f, kPairs);
+  return s;
 }
 
 // round(round32(s * inv) * w) for one pack.
 template <typename T>
 __device__ __forceinline__ uint4 scale(const uint4& s, const uint4& w, float inv) {
-  using P = Pack<T>;
-  float f[P::kElems], g[P::kElems];
-  P::to_f32(s, f);
-  P::to_f32(w, g);
+  constexpr int kPairs = Pack<T>::kElems / 2;
+  const float2 inv2 = make_float2(inv, inv);
+  float2 f[kPairs], g[kPairs];
+  pack_to_pairs<T>(s, f);
+  pack_to_pairs<T>(w, g);
 #pragma unroll
-  for (int e = 0; e < P::kElems; ++e) f[e] = __fmul_rn(__fmul_rn(f[e], inv), g[e]);
-  return P::from_f32(f);
+  for (int i = 0; i < kPairs; ++i) f[i] = __fmul2_rn(__fmul2_rn(f[i], inv2), g[i]);
+  return pairs_to_pack<T>(f);
 }
 
 // ---- warp family -----------------------------------------------------------
@@ -111,17 +114,13 @@ __global__ void __launch_bounds__(256) row_norm_warp_kernel(RowArgs<T> a) {
         if constexpr (kAdd) r[i] = load16(a.residual + base + static_cast<int64_t>(c) * E);
       }
     }
-    float sum_sq = 0.0f;
+    float2 acc = make_float2(0.0f, 0.0f);
 #pragma unroll
     for (int i = 0; i < kPacksPerLane; ++i) {
       const int c = lane + i * kWarpSize;
-      if (c < packs) {
-        float f[E];
-        s[i] = combine<T, kAdd>(s[i], r[i], f);
-        sum_sq = accumulate_squares(sum_sq, f, E);
-      }
+      if (c < packs) s[i] = combine<T, kAdd>(s[i], r[i], acc);
     }
-    sum_sq = group_allreduce_sum<kWarpSize>(sum_sq);
+    const float sum_sq = group_allreduce_sum<kWarpSize>(__fadd_rn(acc.x, acc.y));
     const float inv = inverse_rms(sum_sq, n, a.epsilon);
 #pragma unroll
     for (int i = 0; i < kPacksPerLane; ++i) {
@@ -179,17 +178,14 @@ __global__ void __launch_bounds__(kMaxThreads) row_norm_cta_kernel(RowArgs<T> a)
         if constexpr (kAdd) r[i] = load16(a.residual + base + static_cast<int64_t>(c) * E);
       }
     }
-    float sum_sq = 0.0f;
+    float2 acc = make_float2(0.0f, 0.0f);
 #pragma unroll
     for (int i = 0; i < kPacksPerThread; ++i) {
       const int c = threadIdx.x + i * blockDim.x;
-      if (c < packs) {
-        float f[E];
-        s[i] = combine<T, kAdd>(s[i], r[i], f);
-        sum_sq = accumulate_squares(sum_sq, f, E);
-      }
+      if (c < packs) s[i] = combine<T, kAdd>(s[i], r[i], acc);
     }
-    const float inv = inverse_rms(block_allreduce_sum(sum_sq, partial, parity), n, a.epsilon);
+    const float inv = inverse_rms(block_allreduce_sum(__fadd_rn(acc.x, acc.y), partial, parity),
+                                  n, a.epsilon);
     parity ^= 1;
 #pragma unroll
     for (int i = 0; i < kPacksPerThread; ++i) {
@@ -215,17 +211,16 @@ __global__ void __launch_bounds__(1024) row_norm_wide_kernel(RowArgs<T> a) {
   int parity = 0;
   for (int64_t row = blockIdx.x; row < a.rows; row += gridDim.x) {
     const int64_t base = row * a.hidden;
-    float sum_sq = 0.0f;
+    float2 acc = make_float2(0.0f, 0.0f);
     for (int c = threadIdx.x; c < packs; c += blockDim.x) {
       const int64_t off = base + static_cast<int64_t>(c) * E;
       uint4 r;
       if constexpr (kAdd) r = load16(a.residual + off);
-      float f[E];
-      const uint4 s = combine<T, kAdd>(load16(a.input + off), r, f);
+      const uint4 s = combine<T, kAdd>(load16(a.input + off), r, acc);
       if constexpr (kAdd) store16(a.residual_output + off, s);
-      sum_sq = accumulate_squares(sum_sq, f, E);
     }
-    const float inv = inverse_rms(block_allreduce_sum(sum_sq, partial, parity), n, a.epsilon);
+    const float inv = inverse_rms(block_allreduce_sum(__fadd_rn(acc.x, acc.y), partial, parity),
+                                  n, a.epsilon);
     parity ^= 1;
     // Pass 2 re-reads exactly the packs this thread handled in pass 1.
     const T* source = kAdd ? a.residual_output : a.input;
@@ -329,19 +324,17 @@ __global__ void __launch_bounds__(1024) row_norm_bulk_kernel(RowArgs<T> a, int s
     const bool arrived = mbarrier_wait_bounded(&stage_full[s], phase);
     const unsigned char* stage = stage_memory + static_cast<size_t>(s) * stage_bytes;
     uint4 v[kPacksPerThread];
-    float sum_sq = 0.0f;
+    float2 acc = make_float2(0.0f, 0.0f);
 #pragma unroll
     for (int k = 0; k < kPacksPerThread; ++k) {
       const int c = threadIdx.x + k * blockDim.x;
       if (c < packs) {
         uint4 r;
         if constexpr (kAdd) r = load16_shared(stage + row_bytes + static_cast<uint32_t>(c) * 16);
-        float f[E];
-        v[k] = combine<T, kAdd>(load16_shared(stage + static_cast<uint32_t>(c) * 16), r, f);
-        sum_sq = accumulate_squares(sum_sq, f, E);
+        v[k] = combine<T, kAdd>(load16_shared(stage + static_cast<uint32_t>(c) * 16), r, acc);
       }
     }
-    sum_sq = group_allreduce_sum<kWarpSize>(sum_sq);
+    const float sum_sq = group_allreduce_sum<kWarpSize>(__fadd_rn(acc.x, acc.y));
     if (lane == 0) partial[i & 1][warp] = sum_sq;
     if (__syncthreads_or(!arrived)) {
       // A copy never completed within the bound: record it, give copies still
@@ -663,7 +656,10 @@ extern "C" int sm120n_get_device_faults(uint32_t* out_count) {
   if (err != cudaSuccess) {
     return fail(SM120N_ERR_CUDA, "reading the fault counter failed: %s", cudaGetErrorString(err));
   }
-  *out_count = value;
+  unsigned int heads = 0;
+  const int rc = read_head_faults(&heads);
+  if (rc != SM120N_OK) return rc;
+  *out_count = value + heads;
   return SM120N_OK;
 }
 
@@ -674,5 +670,5 @@ extern "C" int sm120n_reset_device_faults(void) {
   if (err != cudaSuccess) {
     return fail(SM120N_ERR_CUDA, "resetting the fault counter failed: %s", cudaGetErrorString(err));
   }
-  return SM120N_OK;
+  return reset_head_faults();
 }

@@ -5,12 +5,17 @@ Tolerances (the bar every parity test states):
     dtype for bf16 / fp16, at most 4 ulp for fp32, measured as the distance
     between the two values on the dtype's ordered bit lattice. Residual
     outputs (round(x + r)) must be bit-exact.
-  * RoPE outputs: the norm-stage bar (k ulp on each normalised value n that
-    enters the rotation) propagated through it, plus k ulp of the output:
-      |actual - expected| <= k * (ulp(n_i)|c_i| + ulp(n_j)|s_i| + ulp(y)),
+  * RoPE outputs: the norm-stage bar -- k ulp on t = round(x * inv_rms), the
+    first rounding -- propagated exactly through the later roundings:
+      |dn| <= k * (ulp(t)|w| + ulp(n))           n = round(t * w)
+      |dy| <= |dn_i||c_i| + |dn_j||s_i| + k * ulp(y)
     k = 1 for bf16 / fp16 and 4 for fp32; each ulp is taken at the larger of
-    the exact and the rounded magnitude. Near-zero outputs come from
-    cancellation, so an ulp of the output alone is not a meaningful bar.
+    the exact and the rounded magnitude. The first term matters: the fp32
+    sum of squares may end one ulp apart in a different (equally valid)
+    summation order, which flips the first rounding of a few elements per
+    million, and the weight multiply can carry that flip into 2 ulp of n
+    when t * w crosses a binade. Near-zero outputs come from cancellation,
+    so an ulp of the output alone is not a meaningful bar.
   * KV-cache slots: bit-exact.
 """
 from __future__ import annotations
@@ -83,23 +88,27 @@ def assert_bitwise_equal(actual: torch.Tensor, expected: torch.Tensor, what: str
 def rope_bound(x: torch.Tensor, weight: torch.Tensor, positions: torch.Tensor,
                cos_sin: torch.Tensor, expected: torch.Tensor, k: int | None = None,
                eps: float = 1e-6) -> torch.Tensor:
-    """Propagation part of the RoPE tolerance for a [T, H, D] head tensor:
-    k * (ulp(n_i)|c_i| + ulp(n_j)|s_i|), with n evaluated in fp64 from the
-    inputs and its ulp taken at the larger of its own and its dtype-rounded
-    magnitude (a value just below a power of two may round up into the next
-    binade). assert_rope_close adds k ulp of the output."""
+    """Propagation part of the RoPE tolerance for a [T, H, D] head tensor
+    (module docstring): |dn_i||c_i| + |dn_j||s_i| with
+    |dn| = k * (ulp(t)|w| + ulp(n)), t and n evaluated in fp64 from the inputs.
+    assert_rope_close / rope_violations add k ulp of the output."""
     dtype = expected.dtype
     k = default_rope_k(dtype) if k is None else k
     xd = x.detach().cpu().to(torch.float64)
     d = xd.shape[-1]
     half = d // 2
-    inv = torch.rsqrt(xd.square().mean(-1, keepdim=True) + eps)
-    n = xd * inv * weight.detach().cpu().to(torch.float64)
-    n_ulp = torch.maximum(ulp_at(n, dtype), ulp_at(n.to(dtype).to(torch.float64), dtype))
+    w = weight.detach().cpu().to(torch.float64)
+    t = xd * torch.rsqrt(xd.square().mean(-1, keepdim=True) + eps)
+    n = t * w
+
+    def ulp_rounded(v):
+        return torch.maximum(ulp_at(v, dtype), ulp_at(v.to(dtype).to(torch.float64), dtype))
+
+    dn = k * (ulp_rounded(t) * w.abs() + ulp_rounded(n))
     rows = cos_sin.detach().cpu().reshape(-1, d).to(torch.float64)[positions.cpu().long()]
     c, s = rows[:, None, :half].abs(), rows[:, None, half:].abs()
-    u1, u2 = n_ulp[..., :half], n_ulp[..., half:]
-    return k * torch.cat((u1 * c + u2 * s, u2 * c + u1 * s), dim=-1)
+    d1, d2 = dn[..., :half], dn[..., half:]
+    return torch.cat((d1 * c + d2 * s, d2 * c + d1 * s), dim=-1)
 
 
 def default_rope_k(dtype: torch.dtype) -> int:

@@ -51,7 +51,7 @@ def test_qk_double_rounding_versus_the_reference_kernel(dtype):
     k = rand((tokens, 8, 128), dtype, 5)
     v = rand((tokens, 8, 128), dtype, 6)
     qw, kw = rand((128,), dtype, 7, 1.0, 0.1), rand((128,), dtype, 8, 1.0, 0.1)
-    pos = torch.randperm(4096, device="cuda")[:tokens]
+    pos = torch.randperm(4096, generator=torch.Generator().manual_seed(9))[:tokens].cuda()
     inv = 1.0 / (1e6 ** (torch.arange(0, 128, 2, dtype=torch.float32, device="cuda") / 128))
     f = torch.outer(torch.arange(4096, dtype=torch.float32, device="cuda"), inv)
     cache = torch.cat((f.cos(), f.sin()), dim=-1)
