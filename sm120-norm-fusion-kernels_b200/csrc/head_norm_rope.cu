@@ -377,201 +377,6 @@ __global__ void __launch_bounds__(256, sizeof(T) == 2 ? 4 : 2) head_norm_rope_ke
   }
 }
 
-// ---- bulk variant: tokens staged through shared memory by the TMA engine ---
-// Persistent blocks; block b owns tokens b, b + gridDim.x, ... and keeps up to
-// `stages` of them in flight. Thread 0 copies a token's Q heads, K heads,
-// V heads (contiguous per token) and its 512-byte cos/sin row into a stage
-// with cp.async.bulk, completion counted by the stage's mbarrier. Positions
-// and slots are prefetched for 256 tokens at a time into shared memory, so the
-// issuing thread never waits on a dependent load. Every lane group processes
-// heads out of the stage and stores results straight from registers; the
-// block barrier that ends a token also proves the stage has been read, and
-// thread 0 then refills it with the token `stages` ahead.
-__device__ unsigned int g_expired_waits_heads = 0;
-
-constexpr int kMaxTokenStages = 8;
-constexpr int kPrefetch = 256;  // tokens per position / slot prefetch (= block size)
-
-template <typename T, bool kStoreKV>
-__global__ void __launch_bounds__(256) head_norm_rope_bulk_kernel(HeadArgs<T> a, int stages) {
-  extern __shared__ __align__(128) unsigned char stage_memory[];
-  __shared__ __align__(8) uint64_t stage_full[kMaxTokenStages];
-  __shared__ int64_t stage_position[kMaxTokenStages];
-  __shared__ int64_t stage_slot[kMaxTokenStages];
-  __shared__ int64_t prefetch_position[2][kPrefetch];
-  __shared__ int32_t prefetch_slot[2][kPrefetch];
-
-  const int lane = threadIdx.x & (kWarpSize - 1);
-  const int part = lane % kLanesPerHead;
-  const int head_in_warp = lane / kLanesPerHead;
-  const int warp = threadIdx.x / kWarpSize;
-  const int warps = blockDim.x / kWarpSize;
-  const int lo = part * kElemsPerHalf;
-  const int hi = kHalf + lo;
-  const int heads = a.query_heads + a.key_heads;
-  constexpr uint32_t kHeadBytes = kHeadDim * sizeof(T);
-  const uint32_t q_bytes = static_cast<uint32_t>(a.query_heads) * kHeadBytes;
-  const uint32_t k_bytes = static_cast<uint32_t>(a.key_heads) * kHeadBytes;
-  const uint32_t v_bytes = kStoreKV ? k_bytes : 0;
-  const uint32_t rope_offset = q_bytes + k_bytes + v_bytes;
-  const uint32_t stage_bytes = rope_offset + kHeadDim * sizeof(float);
-  const int64_t first_token = blockIdx.x;
-  const int64_t my_tokens =
-      first_token < a.tokens ? (a.tokens - first_token + gridDim.x - 1) / gridDim.x : 0;
-
-  if (threadIdx.x == 0) {
-    for (int s = 0; s < stages; ++s) mbarrier_init(&stage_full[s], 1);
-    fence_mbarrier_init();
-  }
-  __syncthreads();
-  wait_for_upstream_grid();
-  release_downstream_grid();
-
-  auto token_of = [&](int64_t j) { return first_token + j * gridDim.x; };
-  auto prefetch = [&](int64_t chunk) {  // every thread: one token of the chunk
-    const int64_t j = chunk * kPrefetch + threadIdx.x;
-    if (threadIdx.x < kPrefetch && j < my_tokens) {
-      const int64_t t = token_of(j);
-      prefetch_position[chunk & 1][threadIdx.x] = a.positions[t];
-      if constexpr (kStoreKV) {  // slot_mapping may be absent when there are no KV heads
-        prefetch_slot[chunk & 1][threadIdx.x] = a.key_heads > 0 ? a.slots[t] : -1;
-      }
-    }
-  };
-  auto fill = [&](int64_t j) {  // thread 0
-    const int s = static_cast<int>(j % stages);
-    const int64_t t = token_of(j);
-    const int64_t position = prefetch_position[(j / kPrefetch) & 1][j % kPrefetch];
-    const int64_t slot = kStoreKV ? prefetch_slot[(j / kPrefetch) & 1][j % kPrefetch] : -1;
-    const bool rope = position >= 0 && position < a.rope_positions;
-    stage_position[s] = position;
-    stage_slot[s] = slot;
-    unsigned char* dst = stage_memory + static_cast<size_t>(s) * stage_bytes;
-    mbarrier_arrive_expect_tx(&stage_full[s],
-                              rope_offset + (rope ? kHeadDim * sizeof(float) : 0));
-    if (q_bytes) bulk_load(dst, a.query + t * a.query_heads * kHeadDim, q_bytes, &stage_full[s]);
-    if (k_bytes) bulk_load(dst + q_bytes, a.key + t * a.key_heads * kHeadDim, k_bytes, &stage_full[s]);
-    if (v_bytes) {
-      bulk_load(dst + q_bytes + k_bytes, a.value + t * a.key_heads * kHeadDim, v_bytes,
-                &stage_full[s]);
-    }
-    if (rope) {
-      bulk_load(dst + rope_offset, a.cos_sin + position * kHeadDim, kHeadDim * sizeof(float),
-                &stage_full[s]);
-    }
-  };
-
-  prefetch(0);
-  __syncthreads();
-  if (threadIdx.x == 0) {
-    for (int64_t j = 0; j < my_tokens && j < stages; ++j) fill(j);
-  }
-  const Half8<T> qw_lo = load_half<T, true>(a.query_weight + lo);
-  const Half8<T> qw_hi = load_half<T, true>(a.query_weight + hi);
-  const Half8<T> kw_lo = load_half<T, true>(a.key_weight + lo);
-  const Half8<T> kw_hi = load_half<T, true>(a.key_weight + hi);
-
-  for (int64_t j = 0; j < my_tokens; ++j) {
-    if (j % kPrefetch == 0 && (j / kPrefetch + 1) * kPrefetch < my_tokens) {
-      prefetch(j / kPrefetch + 1);  // read by thread 0 only after later barriers
-    }
-    const int s = static_cast<int>(j % stages);
-    const bool arrived =
-        mbarrier_wait_bounded(&stage_full[s], static_cast<uint32_t>((j / stages) & 1));
-    const unsigned char* stage = stage_memory + static_cast<size_t>(s) * stage_bytes;
-    const int64_t t = token_of(j);
-    const int64_t position = stage_position[s];
-    const int64_t slot = stage_slot[s];
-    const bool rope = arrived && position >= 0 && position < a.rope_positions;
-    const bool store_kv = kStoreKV && slot >= 0 && slot < a.cache_slots;
-    float2 c[4], sn[4];
-    if (rope) {
-      load8_pairs<true>(reinterpret_cast<const float*>(stage + rope_offset) + lo, c);
-      load8_pairs<true>(reinterpret_cast<const float*>(stage + rope_offset) + hi, sn);
-    }
-    for (int base = warp * kHeadsPerWarp; base < heads; base += warps * kHeadsPerWarp) {
-      const int h = base + head_in_warp;
-      const bool active = h < heads;
-      const bool is_query = h < a.query_heads;
-      const int kv_head = h - a.query_heads;
-      const uint32_t in_stage = is_query ? h * kHeadBytes : q_bytes + kv_head * kHeadBytes;
-      Half8<T> x_lo{}, x_hi{};
-      if (active) {
-        x_lo = load_half<T, true>(reinterpret_cast<const T*>(stage + in_stage) + lo);
-        x_hi = load_half<T, true>(reinterpret_cast<const T*>(stage + in_stage) + hi);
-      }
-      float2 acc = half_sum_squares<T>(x_hi, half_sum_squares<T>(x_lo, make_float2(0.f, 0.f)));
-      const float total = group_allreduce_sum<kLanesPerHead>(__fadd_rn(acc.x, acc.y));  // all lanes
-      if (!active || !rope) continue;
-      const float inv = head_inverse_rms(make_float2(total, 0.0f), a.epsilon);
-      const Half8<T> n_lo = normalise_half<T>(x_lo, select_half<T>(is_query, qw_lo, kw_lo), inv);
-      const Half8<T> n_hi = normalise_half<T>(x_hi, select_half<T>(is_query, qw_hi, kw_hi), inv);
-      Half8<T> out_lo, out_hi;
-      rotate_half<T>(n_lo, n_hi, c, sn, out_lo, out_hi);
-      T* head = is_query ? a.query + (t * a.query_heads + h) * kHeadDim
-                         : a.key + (t * a.key_heads + kv_head) * kHeadDim;
-      store_half<T, true>(head + lo, out_lo);
-      store_half<T, true>(head + hi, out_hi);
-      if constexpr (kStoreKV) {
-        if (!is_query && store_kv) {
-          const int64_t cache_head = (slot * a.key_heads + kv_head) * kHeadDim;
-          const T* v = reinterpret_cast<const T*>(stage + q_bytes + k_bytes + kv_head * kHeadBytes);
-          store_half<T, true>(a.key_cache + cache_head + lo, out_lo);  // same bits as K
-          store_half<T, true>(a.key_cache + cache_head + hi, out_hi);
-          store_half<T, true>(a.value_cache + cache_head + lo, load_half<T, true>(v + lo));
-          store_half<T, true>(a.value_cache + cache_head + hi, load_half<T, true>(v + hi));
-        }
-      }
-    }
-    if (__syncthreads_or(!arrived)) {
-      // A copy never completed within the bound: record it, give copies still
-      // in flight a bounded chance to land, and leave this block's tokens.
-      if (threadIdx.x == 0) {
-        atomicAdd(&g_expired_waits_heads, 1u);
-        for (int64_t i = j; i < my_tokens && i < j + stages; ++i) {
-          mbarrier_wait_bounded(&stage_full[i % stages], static_cast<uint32_t>((i / stages) & 1));
-        }
-      }
-      __syncthreads();
-      return;
-    }
-    if (threadIdx.x == 0 && j + stages < my_tokens) {
-      fence_async_shared();  // this stage's shared-memory reads before the refill
-      fill(j + stages);
-    }
-  }
-}
-
-// Launches the bulk variant when its stages fit; *launched reports whether.
-template <typename T, bool kStoreKV>
-int launch_heads_bulk(const HeadArgs<T>& a, cudaStream_t stream, bool* launched) {
-  *launched = false;
-  const size_t stage_bytes =
-      static_cast<size_t>(a.query_heads + a.key_heads + (kStoreKV ? a.key_heads : 0)) *
-          kHeadDim * sizeof(T) + kHeadDim * sizeof(float);
-  size_t block_smem = 0;
-  int rc = max_block_smem(&block_smem);
-  if (rc != SM120N_OK) return rc;
-  const size_t static_smem = 8 * 1024;  // barriers, per-stage indices, prefetch arrays
-  int stages = static_cast<int>(std::min<size_t>(kMaxTokenStages, (64 * 1024) / stage_bytes));
-  stages = std::max(stages, 2);
-  if (stages * stage_bytes + static_smem > block_smem) return SM120N_OK;
-  const size_t smem = stages * stage_bytes;
-  auto kernel = head_norm_rope_bulk_kernel<T, kStoreKV>;
-  rc = allow_dynamic_smem(reinterpret_cast<const void*>(kernel), smem);
-  if (rc != SM120N_OK) return rc;
-  DeviceInfo dev;
-  rc = current_device_info(&dev);
-  if (rc != SM120N_OK) return rc;
-  int resident = 1;
-  rc = max_resident_ctas(reinterpret_cast<const void*>(kernel), 256, smem, &resident);
-  if (rc != SM120N_OK) return rc;
-  const int64_t grid = std::max<int64_t>(
-      1, std::min<int64_t>(a.tokens, static_cast<int64_t>(dev.sm_count) * resident));
-  *launched = true;
-  return launch(kernel, dim3(static_cast<unsigned>(grid)), dim3(256), smem, stream, a, stages);
-}
-
 // threads_per_block == 0 selects the B200 default: up to 256 threads and a
 // persistent grid capped at what is resident on the device.
 template <typename T, bool kStoreKV>
@@ -584,13 +389,6 @@ int run_heads(HeadArgs<T> a, int threads_per_block, cudaStream_t stream) {
   DeviceInfo dev;
   int rc = current_device_info(&dev);
   if (rc != SM120N_OK) return rc;
-  // Many tokens: stage them through shared memory (bulk copies); the default
-  // launch only, the fixed-shape versions keep the register kernel.
-  if (vector && threads_per_block == 0 && a.tokens >= 2 * static_cast<int64_t>(dev.sm_count)) {
-    bool launched = false;
-    rc = launch_heads_bulk<T, kStoreKV>(a, stream, &launched);
-    if (rc != SM120N_OK || launched) return rc;
-  }
   auto kernel = vector ? head_norm_rope_kernel<T, kStoreKV, true>
                        : head_norm_rope_kernel<T, kStoreKV, false>;
   const int64_t heads_per_warp = kHeadsPerWarp;
@@ -678,23 +476,6 @@ int check_heads(int64_t tokens, int64_t query_heads, int64_t key_heads, int64_t 
 }
 
 }  // namespace
-
-int read_head_faults(unsigned int* out) {
-  const cudaError_t err = cudaMemcpyFromSymbol(out, g_expired_waits_heads, sizeof *out);
-  if (err != cudaSuccess) {
-    return fail(SM120N_ERR_CUDA, "reading the fault counter failed: %s", cudaGetErrorString(err));
-  }
-  return SM120N_OK;
-}
-
-int reset_head_faults() {
-  const unsigned int zero = 0;
-  const cudaError_t err = cudaMemcpyToSymbol(g_expired_waits_heads, &zero, sizeof zero);
-  if (err != cudaSuccess) {
-    return fail(SM120N_ERR_CUDA, "resetting the fault counter failed: %s", cudaGetErrorString(err));
-  }
-  return SM120N_OK;
-}
 
 }  // namespace sm120n
 

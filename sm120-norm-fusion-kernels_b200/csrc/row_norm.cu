@@ -656,10 +656,7 @@ extern "C" int sm120n_get_device_faults(uint32_t* out_count) {
   if (err != cudaSuccess) {
     return fail(SM120N_ERR_CUDA, "reading the fault counter failed: %s", cudaGetErrorString(err));
   }
-  unsigned int heads = 0;
-  const int rc = read_head_faults(&heads);
-  if (rc != SM120N_OK) return rc;
-  *out_count = value + heads;
+  *out_count = value;
   return SM120N_OK;
 }
 
@@ -670,5 +667,5 @@ extern "C" int sm120n_reset_device_faults(void) {
   if (err != cudaSuccess) {
     return fail(SM120N_ERR_CUDA, "resetting the fault counter failed: %s", cudaGetErrorString(err));
   }
-  return reset_head_faults();
+  return SM120N_OK;
 }

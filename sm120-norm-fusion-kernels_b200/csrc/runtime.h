@@ -40,10 +40,6 @@ int allow_dynamic_smem(const void* kernel, size_t bytes);
 // Shared memory a block may use on the current device (opt-in maximum).
 int max_block_smem(size_t* bytes);
 
-// Expired bounded waits recorded by the bulk Q/K kernels (head_norm_rope.cu).
-int read_head_faults(unsigned int* out);
-int reset_head_faults();
-
 // Launch `kernel` on `stream`, with the programmatic-stream-serialisation
 // attribute when enabled.
 template <typename... KernelArgs, typename... Args>
