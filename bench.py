@@ -327,6 +327,9 @@ def gpu_arm(args, dist: Dist) -> dict:
     clocks.__enter__()
     try:
         step_ms = sweep_step_ms(ops, data, flush, args.steps, args.warmup, dist)
+        if args.step_only:  # the timed steps alone (for a launch-list capture)
+            return {"metric": "step only", "ms_per_step": round(dist.max(step_ms), 5),
+                    "gpu_launches": launches_per_step * args.steps}
         line = _measure_rest(args, dist, ops, flush, data, step_ms, launches_per_step)
     finally:
         clocks.__exit__(None, None, None)
@@ -649,7 +652,8 @@ def profile_case(args) -> None:
                                                     args.version or 2)
     flush = Flusher()
     for _ in range(args.launches):
-        flush()
+        if not args.warm:  # --warm: inputs stay L2-resident, as in a decode loop
+            flush()
         fn()
     torch.cuda.synchronize()
     print(f"profile: {args.profile} {args.dtype} tokens={t} hidden={h} heads={args.heads} "
@@ -666,6 +670,8 @@ def main():
     parser.add_argument("--cpu-seconds", type=float, default=10.0)
     parser.add_argument("--skip-per-op", action="store_true")
     parser.add_argument("--skip-cpu", action="store_true")
+    parser.add_argument("--step-only", action="store_true",
+                        help="run warm-up and the timed steps only (launch-list captures)")
     parser.add_argument("--profile", choices=["fused", "rms", "qkkv", "qk"],
                         help="launch one operator at one shape and exit (ncu driver)")
     parser.add_argument("--tokens", type=int, default=1024)
@@ -674,6 +680,8 @@ def main():
     parser.add_argument("--dtype", default="bf16", choices=["bf16", "fp16", "fp32"])
     parser.add_argument("--version", type=int, default=0)
     parser.add_argument("--launches", type=int, default=5)
+    parser.add_argument("--warm", action="store_true",
+                        help="with --profile: no L2 flush between launches")
     args = parser.parse_args()
     if args.profile:
         profile_case(args)
@@ -701,7 +709,7 @@ def main():
     dist.init()
     try:
         line = gpu_arm(args, dist)
-        if dist.rank == 0 and dist.world == 1 and not args.skip_cpu:
+        if dist.rank == 0 and dist.world == 1 and not args.skip_cpu and not args.step_only:
             threads = host_threads()
             gbs, passes, elapsed = cpu_sweep_gbs(args.cpu_seconds, threads)
             line["cpu_baseline"] = {
