@@ -369,29 +369,54 @@ def _measure_rest(args, dist, ops, flush, data, step_ms, launches_per_step) -> d
             for hx, hr in host]
     h2d = sum(2 * hx.numel() * hx.element_size() for hx, _ in host)
 
-    def e2e_step():
-        for (t, h, name, x, r, w), (hx, hr), (ox, orr) in zip(data.items, host, outs):
-            x.copy_(hx, non_blocking=True)
-            r.copy_(hr, non_blocking=True)
-            ops.fused_add_rms_norm_inplace(x, r, w, EPS)
-            ox.copy_(x, non_blocking=True)
-            orr.copy_(r, non_blocking=True)
+    # Streamed as an engine would: uploads on one stream, the operator on a
+    # second, downloads on a third, so the two PCIe directions overlap across
+    # the step's 48 independent calls; the whole step (copies, calls, the
+    # events between streams) is captured once as a CUDA graph, so the host
+    # issues one launch per step. Steps run one after another (each rewrites
+    # the same device buffers).
+    up, compute, down = torch.cuda.Stream(), torch.cuda.Stream(), torch.cuda.Stream()
 
-    for _ in range(args.warmup):
+    def e2e_step():
+        origin = torch.cuda.current_stream()
+        for stream in (up, compute, down):
+            stream.wait_stream(origin)
+        for (t, h, name, x, r, w), (hx, hr), (ox, orr) in zip(data.items, host, outs):
+            with torch.cuda.stream(up):
+                x.copy_(hx, non_blocking=True)
+                r.copy_(hr, non_blocking=True)
+            compute.wait_stream(up)
+            with torch.cuda.stream(compute):
+                ops.fused_add_rms_norm_inplace(x, r, w, EPS)
+            down.wait_stream(compute)
+            with torch.cuda.stream(down):
+                ox.copy_(x, non_blocking=True)
+                orr.copy_(r, non_blocking=True)
+        for stream in (up, compute, down):
+            origin.wait_stream(stream)
+
+    e2e_step()  # eager once, then capture
+    torch.cuda.synchronize()
+    e2e_graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(e2e_graph):
         e2e_step()
+    for _ in range(args.warmup):
+        e2e_graph.replay()
     dist.barrier()
+    e2e_steps = max(3, args.steps // 5)
     a, b = event_pair()
     a.record()
-    e2e_steps = max(3, args.steps // 5)
     for _ in range(e2e_steps):
-        e2e_step()
+        e2e_graph.replay()
     b.record()
     b.synchronize()
     e2e_ms = dist.max(a.elapsed_time(b) / e2e_steps)
     e2e = {"value": round(data.bytes * dist.world / (e2e_ms * 1e-3) / 1e9, 2), "unit": "GB/s",
            "ms_per_step": round(e2e_ms, 4), "h2d_bytes_per_step": h2d * dist.world,
            "d2h_bytes_per_step": h2d * dist.world,
-           "path": "sm120_rmsnorm.fused_add_rms_norm_inplace with pinned-host copies"}
+           "path": "sm120_rmsnorm.fused_add_rms_norm_inplace with pinned-host copies; uploads, "
+                   "calls and downloads on three streams (both PCIe directions overlap), "
+                   "one CUDA graph per step"}
 
     per_op = {} if args.skip_per_op else per_op_suite(ops, flush, dist, args)
 
@@ -577,6 +602,36 @@ def reference_kernels_gpu(args, dist: Dist) -> dict:
             "per_shape": per_shape, "per_op": per_op}
 
 
+def pytorch_cpu_reference_gbs(steps: int, threads: int) -> dict:
+    """The reference's PyTorch oracle math (residual add + RMSNorm,
+    reference.py:14-24 in the reference project; restated op for op in
+    sm120_rmsnorm/reference.py, loaded here by file path so nothing else of
+    the package is imported) on the host CPU over the sweep."""
+    import importlib.util
+
+    path = ROOT / "sm120-norm-fusion-kernels_b200" / "sm120_rmsnorm" / "reference.py"
+    spec = importlib.util.spec_from_file_location("sweep_reference_math", path)
+    module = importlib.util.module_from_spec(spec)
+    spec.loader.exec_module(module)
+    torch.set_num_threads(threads)
+    g = torch.Generator().manual_seed(4321)
+    items = []
+    for t, h, name in sweep_shapes():
+        dt = DTYPES[name]
+        items.append((torch.randn(t, h, generator=g).to(dt), torch.randn(t, h, generator=g).to(dt),
+                      (1 + 0.1 * torch.randn(h, generator=g)).to(dt)))
+    total = sum(fused_bytes(x.shape[0], x.shape[1], x.element_size()) for x, _, _ in items)
+    for x, r, w in items:
+        module.fused_add_rms_norm_reference(x, r, w, EPS)
+    t0 = time.perf_counter()
+    for _ in range(steps):
+        for x, r, w in items:
+            module.fused_add_rms_norm_reference(x, r, w, EPS)
+    elapsed = time.perf_counter() - t0
+    return {"value": round(total * steps / elapsed / 1e9, 3), "unit": "GB/s", "threads": threads,
+            "sample": f"{steps} passes over the 48-call sweep, {elapsed:.2f} s"}
+
+
 def reference_arm(args, dist: Dist) -> dict:
     """The reference path's CPU implementation (C restatement of its PyTorch
     oracle) on the host cores, on the same sweep; rank 0 only."""
@@ -607,6 +662,7 @@ def reference_arm(args, dist: Dist) -> dict:
         "note": "the reference's CPU path is its PyTorch oracle (sm120_rmsnorm/reference.py), "
                 "which cannot travel; this is its C restatement (oracle/norm_oracle.c), "
                 "pinned to the reference's own outputs by the golden-vector tests",
+        "reference_pytorch_cpu": pytorch_cpu_reference_gbs(max(3, args.steps // 4), threads),
         "reference_kernels_b200": reference_kernels_gpu(args, dist),
     }
 
