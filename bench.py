@@ -419,6 +419,7 @@ def _measure_rest(args, dist, ops, flush, data, step_ms, launches_per_step) -> d
                    "one CUDA graph per step"}
 
     per_op = {} if args.skip_per_op else per_op_suite(ops, flush, dist, args)
+    extensions = {} if args.skip_per_op else extension_suite(flush, dist, args)
 
     return {
         "metric": "achieved HBM GB/s (% of B200 peak) and us/call per op at 1/2/4/8 GPUs",
@@ -435,7 +436,7 @@ def _measure_rest(args, dist, ops, flush, data, step_ms, launches_per_step) -> d
                    "l2": "flushed (512 MiB write) before every timed step and every "
                          "per-launch timing, outside the events"},
         "roofline": roofline, "e2e": e2e, "gpu_launches": launches_per_step * args.steps,
-        "per_shape": per_shape, "per_op": per_op,
+        "per_shape": per_shape, "per_op": per_op, "extensions": extensions,
         "device": torch.cuda.get_device_name(dev),
     }
 
@@ -519,6 +520,200 @@ def per_op_suite(ops, flush: Flusher, dist: Dist, args) -> dict:
     record("fused_add_rms_norm_inplace prefill bf16 65536x8192",
            [lambda: ops.fused_add_rms_norm_inplace(x, r, w, EPS)], fused_bytes(65536, 8192, 2))
     del x, r
+    return out
+
+
+def qk_cache_bytes(t: int, hq: int, hk: int, s: int, d: int = 128, rotary: int = 128,
+                   cache_elem: int | None = None) -> int:
+    # as qk_kv_bytes, with the two cache stores at the cache element size
+    cache_elem = s if cache_elem is None else cache_elem
+    return (t * (s * d * (2 * hq + 3 * hk) + 2 * cache_elem * d * hk + 8 + 4 + 4 * rotary)
+            + 2 * d * s)
+
+
+def norm_quant_bytes(t: int, h: int, s: int, add: bool, dynamic: bool) -> int:
+    # x read (and r read + written), fp8 result written, weight once, scales
+    return t * h * s * (3 if add else 1) + t * h + h * s + (4 * t if dynamic else 0)
+
+
+def vllm_ops():
+    """torch.ops._C / _C_cache_ops from the installed vLLM build, as an
+    industrial comparator (never on the product path), or None."""
+    try:
+        import importlib.util
+        spec = importlib.util.find_spec("vllm")
+        if spec is None or not spec.submodule_search_locations:
+            return None
+        root = Path(list(spec.submodule_search_locations)[0])
+        for name in ("_C.abi3.so", "_C_stable_libtorch.abi3.so"):  # both register ops
+            torch.ops.load_library(str(root / name))
+        return torch.ops._C, torch.ops._C_cache_ops
+    except Exception:  # noqa: BLE001 - a missing comparator is reported, not fatal
+        return None
+
+
+def extension_suite(flush: Flusher, dist: Dist, args) -> dict:
+    """The engine-side extensions (sm120_rmsnorm.extensions) at decode and
+    prefill shapes, each beside the unfused vLLM pair that does the same work
+    when vLLM's kernels load (timed the same way: graphs of back-to-back calls
+    on distinct buffer sets after an L2 flush)."""
+    from sm120_rmsnorm import extensions as ext
+
+    out = {}
+    reps = max(3, args.reps)
+    g = torch.Generator(device="cuda").manual_seed(123 + dist.rank)
+    cpu_g = torch.Generator().manual_seed(17 + dist.rank)
+    bf = torch.bfloat16
+    vllm = vllm_ops()
+
+    def sets_for(nbytes):
+        return max(1, min(64, (256 << 20) // max(nbytes, 1)))
+
+    def record(name, calls, nbytes, **extra):
+        try:
+            graph, _ = capture(calls)
+            us = dist.max(time_graph(graph, flush, reps) / len(calls))
+            out[name] = {"us": round(us, 3), "bytes": nbytes,
+                         "gbs": round(nbytes / (us * 1e-6) / 1e9, 1), **extra}
+            del graph
+        except Exception as e:  # noqa: BLE001 - only comparators may fail here
+            if not extra.get("comparator"):
+                raise
+            out[name] = {"unavailable": f"{type(e).__name__}: {str(e)[:160]}"}
+            torch.cuda.synchronize()
+
+    def table(n, rotary=128, dtype=torch.float32):
+        inv = 1.0 / (1e6 ** (torch.arange(0, rotary, 2, dtype=torch.float32, device="cuda") / rotary))
+        f = torch.outer(torch.arange(n, dtype=torch.float32, device="cuda"), inv)
+        return torch.cat((f.cos(), f.sin()), dim=-1).to(dtype)
+
+    cache32, cache_bf = table(32768), table(32768, dtype=bf)
+    one = torch.ones(1, device="cuda")
+    qw = (1 + 0.1 * torch.randn(128, device="cuda", generator=g)).to(bf)
+    kw = (1 + 0.1 * torch.randn(128, device="cuda", generator=g)).to(bf)
+
+    def qk_cache_case(name, b, hq, hk, blocks, layout, fp8, contiguous, strided):
+        cache_dtype = torch.float8_e4m3fn if fp8 else bf
+        nbytes = qk_cache_bytes(b, hq, hk, 2, cache_elem=1 if fp8 else 2)
+        n_sets = sets_for(nbytes)
+        shape = (blocks, 16, hk, 128) if layout == "NHD" else (blocks, hk, 16, 128)
+        kc = torch.zeros(shape, device="cuda", dtype=cache_dtype)
+        vc = torch.zeros_like(kc)
+        all_slots = torch.randperm(blocks * 16, generator=cpu_g)[: b * n_sets].to(torch.int32)
+        sets = []
+        for i in range(n_sets):
+            qkv = torch.randn(b, (hq + 2 * hk) * 128, device="cuda", generator=g).to(bf)
+            if contiguous:
+                pos = torch.arange(b, device="cuda")
+                slots = torch.arange(b, device="cuda", dtype=torch.int32)
+            else:
+                pos = torch.randperm(32768, generator=cpu_g)[:b].cuda()
+                slots = all_slots[i * b:(i + 1) * b].cuda()
+            if strided:
+                q = qkv[:, :hq * 128].view(b, hq, 128)
+                k = qkv[:, hq * 128:(hq + hk) * 128].view(b, hk, 128)
+                v = qkv[:, (hq + hk) * 128:].view(b, hk, 128)
+            else:
+                q = qkv[:, :hq * 128].reshape(b, hq, 128).contiguous()
+                k = qkv[:, hq * 128:(hq + hk) * 128].reshape(b, hk, 128).contiguous()
+                v = qkv[:, (hq + hk) * 128:].reshape(b, hk, 128).contiguous()
+            sets.append((qkv, q, k, v, pos, slots))
+        scales = (one, one) if fp8 else (None, None)
+        calls = [lambda q=q, k=k, v=v, pos=pos, slots=slots: ext.qk_norm_rope_cache_(
+            q, k, v, qw, kw, pos, cache32, kc, vc, slots, *scales, True, layout, EPS)
+            for (_, q, k, v, pos, slots) in sets]
+        record(name, calls, nbytes)
+        if vllm is not None and strided and layout == "NHD":
+            C, cache_ops = vllm
+            kv_dtype = "fp8" if fp8 else "auto"
+            vkc = torch.zeros((blocks, 16, hk, 128), device="cuda",
+                              dtype=torch.uint8 if fp8 else bf)
+            vvc = torch.zeros_like(vkc)
+
+            def unfused(qkv, k, v, pos, slots):
+                C.fused_qk_norm_rope(qkv, hq, hk, hk, 128, EPS, qw, kw, cache_bf, True, pos)
+                cache_ops.reshape_and_cache_flash(k, v, vkc, vvc, slots.long(), kv_dtype, one, one)
+
+            calls = [lambda qkv=qkv, k=k, v=v, pos=pos, slots=slots: unfused(qkv, k, v, pos, slots)
+                     for (qkv, _, k, v, pos, slots) in sets]
+            record(name + " [vLLM fused_qk_norm_rope + reshape_and_cache_flash]", calls, nbytes,
+                   comparator=True)
+        del sets, kc, vc
+
+    qk_cache_case("qk_cache decode bf16 B=1024 32/8 strided qkv, fp8 NHD cache",
+                  1024, 32, 8, 65536, "NHD", True, False, True)
+    qk_cache_case("qk_cache decode bf16 B=1024 32/8 strided qkv, bf16 NHD cache",
+                  1024, 32, 8, 65536, "NHD", False, False, True)
+    qk_cache_case("qk_cache decode bf16 B=1 16/8 strided qkv, fp8 NHD cache",
+                  1, 16, 8, 2048, "NHD", True, False, True)
+    qk_cache_case("qk_cache prefill bf16 32768 tokens 64/8 strided qkv, bf16 NHD cache",
+                  32768, 64, 8, 2048, "NHD", False, True, True)
+    qk_cache_case("qk_cache prefill bf16 32768 tokens 64/8 strided qkv, fp8 NHD cache",
+                  32768, 64, 8, 2048, "NHD", True, True, True)
+    qk_cache_case("qk_cache prefill bf16 32768 tokens 64/8, bf16 HND cache",
+                  32768, 64, 8, 2048, "HND", False, True, False)
+
+    # RMSNorm + fp8 quantisation
+    def quant_case(name, t, h, add, dynamic):
+        nbytes = norm_quant_bytes(t, h, 2, add, dynamic)
+        w = (1 + 0.1 * torch.randn(h, device="cuda", generator=g)).to(bf)
+        scale = torch.full((1,), 0.05, device="cuda")
+        sets = []
+        for _ in range(sets_for(nbytes)):
+            x = torch.randn(t, h, device="cuda", generator=g).to(bf)
+            r = torch.randn(t, h, device="cuda", generator=g).to(bf) if add else None
+            res = torch.empty(t, h, device="cuda", dtype=torch.float8_e4m3fn)
+            scales = torch.empty(t, device="cuda") if dynamic else None
+            sets.append((x, r, res, scales))
+
+        def ours(x, r, res, scales):
+            if dynamic:
+                ext.rms_norm_dynamic_per_token_quant(res, x, w, scales, EPS, None, r)
+            elif add:
+                ext.fused_add_rms_norm_static_fp8_quant(res, x, r, w, scale, EPS)
+            else:
+                ext.rms_norm_static_fp8_quant(res, x, w, scale, EPS)
+
+        record(name, [lambda s=s: ours(*s) for s in sets], nbytes)
+        if vllm is not None:
+            C, _ = vllm
+
+            def theirs(x, r, res, scales):
+                if dynamic:
+                    C.rms_norm_dynamic_per_token_quant(res, x, w, scales.view(-1, 1), EPS, None, r)
+                elif add:
+                    C.fused_add_rms_norm_static_fp8_quant(res, x, r, w, scale, EPS)
+                else:
+                    C.rms_norm_static_fp8_quant(res, x, w, scale, EPS)
+
+            record(name + " [vLLM]", [lambda s=s: theirs(*s) for s in sets], nbytes,
+                   comparator=True)
+        del sets
+
+    quant_case("fused_add_rms_norm_static_fp8_quant bf16 1024x4096", 1024, 4096, True, False)
+    quant_case("rms_norm_dynamic_per_token_quant bf16 1024x4096", 1024, 4096, False, True)
+    quant_case("rms_norm_dynamic_per_token_quant + residual bf16 1024x4096", 1024, 4096, True, True)
+    quant_case("fused_add_rms_norm_static_fp8_quant prefill bf16 65536x8192", 65536, 8192, True,
+               False)
+
+    # the headline op beside vLLM's residual add + RMSNorm on the same shapes
+    if vllm is not None:
+        import sm120_rmsnorm as ops
+        C, _ = vllm
+        for t, h in ((1024, 4096), (65536, 8192)):
+            nbytes = fused_bytes(t, h, 2)
+            w = (1 + 0.1 * torch.randn(h, device="cuda", generator=g)).to(bf)
+            sets = [(torch.randn(t, h, device="cuda", generator=g).to(bf),
+                     torch.randn(t, h, device="cuda", generator=g).to(bf))
+                    for _ in range(sets_for(nbytes))]
+            record(f"fused_add_rms_norm_inplace bf16 {t}x{h}",
+                   [lambda x=x, r=r: ops.fused_add_rms_norm_inplace(x, r, w, EPS) for x, r in sets],
+                   nbytes)
+            record(f"fused_add_rms_norm_inplace bf16 {t}x{h} [vLLM fused_add_rms_norm]",
+                   [lambda x=x, r=r: C.fused_add_rms_norm(x, r, w, EPS) for x, r in sets],
+                   nbytes, comparator=True)
+            del sets
+    out["vllm_comparator"] = "loaded" if vllm is not None else "unavailable"
     return out
 
 

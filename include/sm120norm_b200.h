@@ -22,6 +22,13 @@
  *
  * Aliasing: output may equal input and residual_output may equal residual
  * (the in-place form). Any other overlap between buffers is undefined.
+ *
+ * The last two entry points (sm120n_qk_norm_rope_cache,
+ * sm120n_rms_norm_fp8_quant) go beyond the reference's surface: they serve an
+ * inference engine around the same hot path (general head sizes and partial
+ * rotary, Q/K/V as strided views of one QKV projection output, NHD / HND
+ * paged caches, fp8 KV caches, RMSNorm feeding an fp8 GEMM). Their math is
+ * the reference's, generalised; each states its exact definition.
  */
 #ifndef SM120NORM_B200_H_
 #define SM120NORM_B200_H_
@@ -32,7 +39,7 @@
 extern "C" {
 #endif
 
-#define SM120N_ABI_VERSION 1
+#define SM120N_ABI_VERSION 2
 
 #if defined(__GNUC__)
 #define SM120N_API __attribute__((visibility("default")))
@@ -146,6 +153,117 @@ SM120N_API int sm120n_fused_qk_rms_norm_rope_kv(
     const int32_t* slot_mapping, int64_t tokens, int64_t query_heads,
     int64_t key_heads, int64_t head_dim, int64_t rope_positions,
     int64_t cache_slots, int dtype, float epsilon, int version, void* stream);
+
+/* ------------------------------------------------------------------------
+ * Extensions (not in the reference's surface)
+ * ------------------------------------------------------------------------ */
+
+/* Pairing of rotated elements. NEOX: (i, i + rotary_dim/2), the reference's
+ * half split. INTERLEAVED: (2i, 2i + 1). Both use cos/sin index i. */
+typedef enum sm120n_rope_style {
+  SM120N_ROPE_NEOX = 0,
+  SM120N_ROPE_INTERLEAVED = 1
+} sm120n_rope_style;
+
+/* Element type of a KV cache: AUTO = the activation dtype (bit copies),
+ * FP8_E4M3 = float8 e4m3fn, stored as sat(x / scale) rounded to nearest even,
+ * saturating at +-448. */
+typedef enum sm120n_cache_dtype {
+  SM120N_CACHE_AUTO = 0,
+  SM120N_CACHE_FP8_E4M3 = 1
+} sm120n_cache_dtype;
+
+/*
+ * Arguments of sm120n_qk_norm_rope_cache. Sizes and strides in elements.
+ *   query  [tokens, query_heads, head_dim], token t at query + t*query_token_stride,
+ *          heads adjacent (stride head_dim); likewise key and value, so Q, K and
+ *          V may be views into one [tokens, (Hq + 2*Hk) * head_dim] buffer.
+ *   query_weight, key_weight [head_dim]; positions int64 [tokens];
+ *   cos_sin_cache fp32 [rope_positions, rotary_dim] (cos | sin halves).
+ *   key_cache / value_cache: NULL for no store. Slot s = slot_mapping[t] in
+ *   [0, num_blocks * block_size) goes to block s / block_size, offset
+ *   s % block_size; head h of that slot starts at
+ *     block * cache_block_stride + offset * cache_slot_stride + h * cache_head_stride
+ *   in both caches (NHD [blocks, block_size, Hk, D]: strides (block_size*Hk*D,
+ *   Hk*D, D); HND [blocks, Hk, block_size, D]: (Hk*block_size*D, D,
+ *   block_size*D)). Other slots write nothing.
+ *   k_scale / v_scale: device fp32 scalars, required for FP8_E4M3 caches.
+ */
+typedef struct sm120n_qk_cache_args {
+  uint32_t struct_size; /* sizeof(sm120n_qk_cache_args) */
+  int32_t dtype;        /* sm120n_dtype of Q, K, V and the weights */
+  int64_t tokens;
+  int64_t query_heads;
+  int64_t key_heads;
+  int64_t head_dim;   /* 64, 128 or 256 */
+  int64_t rotary_dim; /* multiple of 16 in [16, head_dim] */
+  int32_t rope_style; /* sm120n_rope_style */
+  int32_t cache_dtype; /* sm120n_cache_dtype */
+  void* query;
+  int64_t query_token_stride;
+  void* key;
+  int64_t key_token_stride;
+  const void* value;
+  int64_t value_token_stride;
+  const void* query_weight;
+  const void* key_weight;
+  const int64_t* positions;
+  const float* cos_sin_cache;
+  int64_t rope_positions;
+  void* key_cache;
+  void* value_cache;
+  const int32_t* slot_mapping;
+  int64_t num_blocks;
+  int64_t block_size;
+  int64_t cache_block_stride;
+  int64_t cache_slot_stride;
+  int64_t cache_head_stride;
+  const float* k_scale;
+  const float* v_scale;
+  float epsilon;
+} sm120n_qk_cache_args;
+
+/*
+ * Generalised Q/K RMSNorm + RoPE + KV store, in place on query and key:
+ *   n = round(round(x * inv_rms(x)) * w) over all head_dim elements,
+ *   the first rotary_dim elements rotated in fp32 as in
+ *   sm120n_fused_qk_rms_norm_rope (style chosen by rope_style), the rest
+ *   passed through as n, everything rounded to the activation dtype;
+ *   then, with caches, key_cache[slot, h] = rotated key (AUTO: bit copy),
+ *   value_cache[slot, h] = value. With head_dim = rotary_dim = 128, NEOX,
+ *   dense strides and an AUTO NHD cache this is bit-identical to
+ *   sm120n_fused_qk_rms_norm_rope_kv. Tokens with positions outside
+ *   [0, rope_positions) are left unchanged and store nothing.
+ * Generalises csrc/rmsnorm_kernels.cu:611-709 (fused_qk_rms_norm_rope_kv_cuda),
+ * whose checks :632-633 restrict it to head_dim 128 and a dense NHD cache.
+ */
+SM120N_API int sm120n_qk_norm_rope_cache(const sm120n_qk_cache_args* args, void* stream);
+
+/*
+ * RMSNorm (optionally after a residual add) with an fp8 e4m3fn output:
+ *   s = residual ? round(input + residual) : input   (residual_output = s)
+ *   y = round(s * inv_rms(s) * weight)                (sm120n_rms_norm's y)
+ *   static  (scale != NULL):  q = sat(y * (1 / scale[0]))
+ *   dynamic (scale == NULL):  a = max|y| of the row (min(a, scale_ub[0]) when
+ *                             scale_ub != NULL); token_scales[row] =
+ *                             max(a / 448, 1 / (448 * 512));
+ *                             q = sat(y * (1 / token_scales[row]))
+ *   sat(v): v clamped to [-448, 448] and rounded to the nearest e4m3fn value
+ *   (ties to even); 1 / x is the correctly rounded fp32 reciprocal.
+ * y follows the rounding sequence of sm120n_rms_norm / sm120n_fused_add_rms_norm
+ * (only the order of the fp32 sum of squares may differ); y itself is not
+ * written. output is [rows, hidden_size] bytes; residual_output may equal
+ * residual.
+ * No reference counterpart: the fp8 activation quantisation that follows
+ * rms_norm_out_cuda (csrc/rmsnorm_kernels.cu:482-524) and
+ * fused_add_rms_norm_out_cuda (:724-801) in an fp8 inference engine.
+ */
+SM120N_API int sm120n_rms_norm_fp8_quant(const void* input, const void* residual,
+                              const void* weight, void* residual_output,
+                              void* output, const float* scale,
+                              float* token_scales, const float* scale_ub,
+                              int64_t rows, int64_t hidden_size, int dtype,
+                              float epsilon, void* stream);
 
 #ifdef __cplusplus
 }

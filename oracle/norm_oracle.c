@@ -10,8 +10,11 @@
  * rounding that PyTorch's CPU kernels apply:
  *   - every fp32 product / sum / difference is rounded to fp32 on its own
  *     (PyTorch evaluates x.float() * inv_rms * weight as separate tensor ops);
- *   - rsqrt(v) is 1 / sqrt(v) with correctly rounded sqrt and divide, and
- *     mean(v) is sum(v) / n (both measured on PyTorch 2.11 CPU);
+ *   - mean(v) is sum(v) / n (PyTorch's CPU mean), and rsqrt(v) is the IEEE
+ *     fp32 1 / sqrt(v): correctly rounded sqrt and divide. PyTorch's
+ *     vectorised CPU sqrt / rsqrt are not correctly rounded on every build
+ *     (on AVX-512 about 0.5% of results differ from it in the last bit), so
+ *     the IEEE form is the reproducible reading of the reference's formula;
  *   - fp32 -> bf16 / fp16 conversions round to nearest even;
  *   - the file is compiled with -ffp-contract=off and without fast-math, so
  *     no product is fused into an FMA and no sum is reassociated;
@@ -114,7 +117,7 @@ static float sum_squares(const float* v, int64_t n) {
   return total;
 }
 
-/* rsqrt(mean(v^2) + eps) as PyTorch CPU evaluates it
+/* rsqrt(mean(v^2) + eps) in IEEE fp32
  * (reference.py:10, :22; F.rms_norm at :38-40). */
 static float inv_rms(const float* v, int64_t n, float eps) {
   float mean = sum_squares(v, n) / (float)n;

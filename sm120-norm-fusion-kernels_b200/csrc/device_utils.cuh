@@ -97,6 +97,17 @@ struct Pack<__half> {
 // fp32x2 instructions (__fadd2_rn / __fmul2_rn / __ffma2_rn: two IEEE
 // round-to-nearest-even operations per instruction, each identical to the
 // scalar one).
+//
+// Contraction: a packed product that feeds a packed sum was measured on B200
+// to come out as one fused multiply-add (a single rounding), even with
+// --fmad=false, unlike the scalar __fmul_rn / __fadd_rn, which are never
+// merged. So the packed forms are used only where no sum consumes a product
+// (products of products, sums of loaded values, deliberate FMAs), and every
+// product-then-sum step uses the scalar intrinsics: product_plus().
+__device__ __forceinline__ float2 product_plus(float2 a, float2 b, float2 c) {
+  return make_float2(__fadd_rn(__fmul_rn(a.x, b.x), c.x), __fadd_rn(__fmul_rn(a.y, b.y), c.y));
+}
+
 template <typename T>
 __device__ __forceinline__ void pack_to_pairs(const uint4& p, float2* f) {
   float g[Pack<T>::kElems];
@@ -117,15 +128,49 @@ __device__ __forceinline__ uint4 pairs_to_pack(const float2* f) {
 }
 
 // Adds the squares of n pairs to a pair of accumulators. For 16-bit storage
-// types x^2 is exact in fp32, so an FMA equals a rounded square followed by a
-// rounded add; fp32 inputs take the separate multiply.
+// types x^2 is exact in fp32, so a packed FMA equals a rounded square followed
+// by a rounded add; fp32 inputs round the square on its own.
 template <typename T>
 __device__ __forceinline__ float2 accumulate_square_pairs(float2 acc, const float2* f, int n) {
 #pragma unroll
   for (int i = 0; i < n; ++i) {
-    acc = sizeof(T) == 2 ? __ffma2_rn(f[i], f[i], acc) : __fadd2_rn(acc, __fmul2_rn(f[i], f[i]));
+    acc = sizeof(T) == 2 ? __ffma2_rn(f[i], f[i], acc) : product_plus(f[i], f[i], acc);
   }
   return acc;
+}
+
+// s = round(x + r) for one pack (kAdd; otherwise s = x), returned packed; its
+// squares are added to `acc` (a pair of accumulators: even and odd elements).
+// The rounded sum is what the reference squares.
+template <typename T, bool kAdd>
+__device__ __forceinline__ uint4 combine_pack(const uint4& x, const uint4& r, float2& acc) {
+  constexpr int kPairs = Pack<T>::kElems / 2;
+  float2 f[kPairs];
+  pack_to_pairs<T>(x, f);
+  uint4 s = x;
+  if constexpr (kAdd) {
+    float2 g[kPairs];
+    pack_to_pairs<T>(r, g);
+#pragma unroll
+    for (int i = 0; i < kPairs; ++i) f[i] = __fadd2_rn(f[i], g[i]);
+    s = pairs_to_pack<T>(f);
+    pack_to_pairs<T>(s, f);
+  }
+  acc = accumulate_square_pairs<T>(acc, f, kPairs);
+  return s;
+}
+
+// round(round32(s * inv) * w) for one pack: the RMSNorm output y.
+template <typename T>
+__device__ __forceinline__ uint4 normalise_pack(const uint4& s, const uint4& w, float inv) {
+  constexpr int kPairs = Pack<T>::kElems / 2;
+  const float2 inv2 = make_float2(inv, inv);
+  float2 f[kPairs], g[kPairs];
+  pack_to_pairs<T>(s, f);
+  pack_to_pairs<T>(w, g);
+#pragma unroll
+  for (int i = 0; i < kPairs; ++i) f[i] = __fmul2_rn(__fmul2_rn(f[i], inv2), g[i]);
+  return pairs_to_pack<T>(f);
 }
 
 // Scalar element access for the unaligned fallback kernels.

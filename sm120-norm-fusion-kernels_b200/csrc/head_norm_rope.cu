@@ -26,7 +26,7 @@
 #include <algorithm>
 #include <type_traits>
 
-#include "device_utils.cuh"
+#include "head_utils.cuh"
 #include "runtime.h"
 
 namespace sm120n {
@@ -35,7 +35,7 @@ namespace {
 constexpr int kHeadDim = 128;
 constexpr int kHalf = kHeadDim / 2;
 constexpr int kLanesPerHead = 8;
-constexpr int kElemsPerHalf = kHalf / kLanesPerHead;  // 8 per lane per half
+static_assert(kHalf / kLanesPerHead == kChunkElems, "one chunk per lane per half");
 constexpr int kHeadsPerWarp = kWarpSize / kLanesPerHead;
 
 template <typename T>
@@ -57,224 +57,9 @@ struct HeadArgs {
   int64_t cache_slots;
   float epsilon;
   // unit -> token division by heads = query_heads + key_heads, for unit
-  // indices below 2^31: q = heads_pow2 ? u >> heads_shift
-  //                                    : umulhi(u, heads_magic) >> (heads_shift - 1)
-  uint32_t heads_magic;
-  int heads_shift;
-  bool heads_pow2;
+  // indices below 2^31
+  HeadDivisor heads_div;
 };
-
-// Constants for dividing indices below 2^31 by d (1 <= d <= 2^20): with
-// l = ceil(log2 d), m = ceil(2^(31+l) / d) satisfies 2^(31+l) <= m*d <=
-// 2^(31+l) + 2^l, so floor(n*m / 2^(31+l)) = floor(n / d) (the round-up
-// method for division by invariant integers).
-template <typename T>
-void set_head_divisor(HeadArgs<T>& a) {
-  const uint32_t d = static_cast<uint32_t>(a.query_heads + a.key_heads);
-  int l = 0;
-  while ((uint64_t{1} << l) < d) ++l;
-  a.heads_shift = l;
-  a.heads_pow2 = (d & (d - 1)) == 0;
-  a.heads_magic = a.heads_pow2 ? 0u
-                               : static_cast<uint32_t>(((uint64_t{1} << (31 + l)) + d - 1) / d);
-}
-
-template <typename T>
-__device__ __forceinline__ uint32_t token_of_unit(const HeadArgs<T>& a, uint32_t unit) {
-  return a.heads_pow2 ? unit >> a.heads_shift
-                      : __umulhi(unit, a.heads_magic) >> (a.heads_shift - 1);
-}
-
-// Eight elements of T as 32-bit words: four words (two elements each) for
-// 16-bit types, eight for fp32. Loaded with 16-byte accesses when the buffers
-// are aligned (kVector), element at a time otherwise.
-template <typename T>
-struct Half8 {
-  static constexpr int kWords = kElemsPerHalf * sizeof(T) / 4;
-  uint32_t w[kWords];
-};
-
-template <typename T, bool kVector>
-__device__ __forceinline__ Half8<T> load_half(const T* p) {
-  Half8<T> h;
-  if constexpr (kVector) {
-#pragma unroll
-    for (int i = 0; i < Half8<T>::kWords / 4; ++i) {
-      const uint4 v = load16(p + i * (16 / sizeof(T)));
-      h.w[4 * i] = v.x;
-      h.w[4 * i + 1] = v.y;
-      h.w[4 * i + 2] = v.z;
-      h.w[4 * i + 3] = v.w;
-    }
-  } else if constexpr (sizeof(T) == 4) {
-#pragma unroll
-    for (int i = 0; i < 8; ++i) h.w[i] = reinterpret_cast<const uint32_t*>(p)[i];
-  } else {
-    const uint16_t* q = reinterpret_cast<const uint16_t*>(p);
-#pragma unroll
-    for (int i = 0; i < 4; ++i) h.w[i] = uint32_t(q[2 * i]) | (uint32_t(q[2 * i + 1]) << 16);
-  }
-  return h;
-}
-
-template <typename T, bool kVector>
-__device__ __forceinline__ void store_half(T* p, const Half8<T>& h) {
-  if constexpr (kVector) {
-#pragma unroll
-    for (int i = 0; i < Half8<T>::kWords / 4; ++i) {
-      store16(p + i * (16 / sizeof(T)),
-              make_uint4(h.w[4 * i], h.w[4 * i + 1], h.w[4 * i + 2], h.w[4 * i + 3]));
-    }
-  } else if constexpr (sizeof(T) == 4) {
-#pragma unroll
-    for (int i = 0; i < 8; ++i) reinterpret_cast<uint32_t*>(p)[i] = h.w[i];
-  } else {
-    uint16_t* q = reinterpret_cast<uint16_t*>(p);
-#pragma unroll
-    for (int i = 0; i < 4; ++i) {
-      q[2 * i] = static_cast<uint16_t>(h.w[i] & 0xffffu);
-      q[2 * i + 1] = static_cast<uint16_t>(h.w[i] >> 16);
-    }
-  }
-}
-
-// Elements (2i, 2i+1) of a half as float2 number i.
-template <typename T>
-__device__ __forceinline__ void unpack_pairs(const Half8<T>& h, float2* f) {
-#pragma unroll
-  for (int i = 0; i < 4; ++i) {
-    if constexpr (sizeof(T) == 4) {
-      f[i] = make_float2(__uint_as_float(h.w[2 * i]), __uint_as_float(h.w[2 * i + 1]));
-    } else {
-      Pack<T>::word_to_f32(h.w[i], f[i].x, f[i].y);
-    }
-  }
-}
-
-template <typename T>
-__device__ __forceinline__ Half8<T> pack_pairs(const float2* f) {
-  Half8<T> h;
-#pragma unroll
-  for (int i = 0; i < 4; ++i) {
-    if constexpr (sizeof(T) == 4) {
-      h.w[2 * i] = __float_as_uint(f[i].x);
-      h.w[2 * i + 1] = __float_as_uint(f[i].y);
-    } else {
-      h.w[i] = Pack<T>::f32_to_word(f[i].x, f[i].y);
-    }
-  }
-  return h;
-}
-
-// Round-to-nearest-even product of two packed pairs. For bf16 and fp16 the
-// fp32 product of two such values is exact, so this single rounding equals
-// the oracle's round(round_fp32(n * w)).
-template <typename T>
-__device__ __forceinline__ uint32_t mul_pair_rn(uint32_t a, uint32_t b);
-template <>
-__device__ __forceinline__ uint32_t mul_pair_rn<__nv_bfloat16>(uint32_t a, uint32_t b) {
-  __nv_bfloat162 r = __hmul2_rn(*reinterpret_cast<__nv_bfloat162*>(&a),
-                                *reinterpret_cast<__nv_bfloat162*>(&b));
-  return *reinterpret_cast<uint32_t*>(&r);
-}
-template <>
-__device__ __forceinline__ uint32_t mul_pair_rn<__half>(uint32_t a, uint32_t b) {
-  __half2 r = __hmul2_rn(*reinterpret_cast<__half2*>(&a), *reinterpret_cast<__half2*>(&b));
-  return *reinterpret_cast<uint32_t*>(&r);
-}
-
-// Sum of squares of a half into a pair of accumulators (even / odd
-// elements), with the sm_100 packed fp32x2 instructions. For 16-bit types x^2
-// is exact in fp32, so the FMA equals the oracle's rounded square followed by
-// a rounded add.
-template <typename T>
-__device__ __forceinline__ float2 half_sum_squares(const Half8<T>& h, float2 acc) {
-  float2 f[4];
-  unpack_pairs<T>(h, f);
-#pragma unroll
-  for (int i = 0; i < 4; ++i) {
-    acc = sizeof(T) == 2 ? __ffma2_rn(f[i], f[i], acc) : __fadd2_rn(acc, __fmul2_rn(f[i], f[i]));
-  }
-  return acc;
-}
-
-// n = round(round(x * inv) * w), the RMSNorm rounded to T and then weighted
-// in T (reference.py:38-41).
-template <typename T>
-__device__ __forceinline__ Half8<T> normalise_half(const Half8<T>& x, const Half8<T>& w,
-                                                   float inv) {
-  const float2 inv2 = make_float2(inv, inv);
-  float2 f[4];
-  unpack_pairs<T>(x, f);
-  if constexpr (sizeof(T) == 4) {
-    float2 g[4];
-    unpack_pairs<T>(w, g);
-#pragma unroll
-    for (int i = 0; i < 4; ++i) f[i] = __fmul2_rn(__fmul2_rn(f[i], inv2), g[i]);
-    return pack_pairs<T>(f);
-  } else {
-    Half8<T> n;
-#pragma unroll
-    for (int i = 0; i < 4; ++i) {
-      const float2 t = __fmul2_rn(f[i], inv2);
-      n.w[i] = mul_pair_rn<T>(Pack<T>::f32_to_word(t.x, t.y), w.w[i]);
-    }
-    return n;
-  }
-}
-
-// Half-split rotation of one lane's pairs: lo = n_lo*c - n_hi*s,
-// hi = n_hi*c + n_lo*s, each product and sum rounded on its own (the
-// subtraction is an add of the negated product, exact under round to nearest
-// even).
-template <typename T>
-__device__ __forceinline__ void rotate_half(const Half8<T>& n_lo, const Half8<T>& n_hi,
-                                            const float2* c, const float2* s,
-                                            Half8<T>& out_lo, Half8<T>& out_hi) {
-  float2 p[4], q[4], y_lo[4], y_hi[4];
-  unpack_pairs<T>(n_lo, p);
-  unpack_pairs<T>(n_hi, q);
-#pragma unroll
-  for (int i = 0; i < 4; ++i) {
-    const float2 qs = __fmul2_rn(q[i], s[i]);
-    y_lo[i] = __fadd2_rn(__fmul2_rn(p[i], c[i]), make_float2(-qs.x, -qs.y));
-    y_hi[i] = __fadd2_rn(__fmul2_rn(q[i], c[i]), __fmul2_rn(p[i], s[i]));
-  }
-  out_lo = pack_pairs<T>(y_lo);
-  out_hi = pack_pairs<T>(y_hi);
-}
-
-// 1 / sqrt(sum_sq / 128 + eps): the mean is a multiply by an exact power of
-// two; the reciprocal is correctly rounded, as a correctly rounded divide of
-// 1 would be.
-__device__ __forceinline__ float head_inverse_rms(float2 acc, float eps) {
-  const float sum = __fadd_rn(acc.x, acc.y);
-  return __frcp_rn(__fsqrt_rn(__fadd_rn(__fmul_rn(sum, 1.0f / kHeadDim), eps)));
-}
-
-template <typename T>
-__device__ __forceinline__ Half8<T> select_half(bool first, const Half8<T>& a, const Half8<T>& b) {
-  Half8<T> r;
-#pragma unroll
-  for (int i = 0; i < Half8<T>::kWords; ++i) r.w[i] = first ? a.w[i] : b.w[i];
-  return r;
-}
-
-// Eight consecutive fp32 values (cos or sin) as four pairs.
-template <bool kVector>
-__device__ __forceinline__ void load8_pairs(const float* p, float2* f) {
-  if constexpr (kVector) {
-    const float4 a = *reinterpret_cast<const float4*>(p);
-    const float4 b = *reinterpret_cast<const float4*>(p + 4);
-    f[0] = make_float2(a.x, a.y);
-    f[1] = make_float2(a.z, a.w);
-    f[2] = make_float2(b.x, b.y);
-    f[3] = make_float2(b.z, b.w);
-  } else {
-#pragma unroll
-    for (int i = 0; i < 4; ++i) f[i] = make_float2(p[2 * i], p[2 * i + 1]);
-  }
-}
 
 // One head of one token, between issuing its loads and finishing it.
 template <typename T>
@@ -295,7 +80,7 @@ __global__ void __launch_bounds__(256, sizeof(T) == 2 ? 4 : 2) head_norm_rope_ke
   const int lane = threadIdx.x & (kWarpSize - 1);
   const int part = lane % kLanesPerHead;       // position of this lane in its head
   const int head_in_warp = lane / kLanesPerHead;
-  const int lo = part * kElemsPerHalf;         // first-half elements [lo, lo + 8)
+  const int lo = part * kChunkElems;         // first-half elements [lo, lo + 8)
   const int hi = kHalf + lo;                   // partners            [hi, hi + 8)
   // The host splits launches so that tokens * heads < 2^31: unit indices fit
   // in 32 bits and the token of a unit is one 32-bit division.
@@ -311,7 +96,7 @@ __global__ void __launch_bounds__(256, sizeof(T) == 2 ? 4 : 2) head_norm_rope_ke
 
   auto begin = [&](HeadJob<T>& job, uint32_t unit) {
     job.active = unit < units;
-    const uint32_t token = job.active ? token_of_unit(a, unit) : 0;
+    const uint32_t token = job.active ? divide(a.heads_div, unit) : 0;
     const int h = job.active ? static_cast<int>(unit - token * heads) : 0;
     job.is_query = h < a.query_heads;
     job.kv_head = h - a.query_heads;
@@ -347,7 +132,7 @@ __global__ void __launch_bounds__(256, sizeof(T) == 2 ? 4 : 2) head_norm_rope_ke
     const float lane_sum = __fadd_rn(acc.x, acc.y);
     const float total = group_allreduce_sum<kLanesPerHead>(lane_sum);  // all lanes, before any exit
     if (!job.active || job.position < 0 || job.position >= a.rope_positions) return;
-    const float inv = head_inverse_rms(make_float2(total, 0.0f), a.epsilon);
+    const float inv = head_inverse_rms<kHeadDim>(make_float2(total, 0.0f), a.epsilon);
     const Half8<T> n_lo =
         normalise_half<T>(job.x_lo, select_half<T>(job.is_query, qw_lo, kw_lo), inv);
     const Half8<T> n_hi =
@@ -396,7 +181,7 @@ int run_heads(HeadArgs<T> a, int threads_per_block, cudaStream_t stream) {
   // 32 bits); larger calls become consecutive launches on the same stream.
   const int64_t max_tokens = ((int64_t{1} << 31) - 1) / heads;
   const int64_t all_tokens = a.tokens;
-  set_head_divisor(a);
+  a.heads_div = make_head_divisor(static_cast<uint32_t>(heads));
   for (int64_t done = 0; done < all_tokens; done += max_tokens) {
     HeadArgs<T> c = a;
     c.tokens = std::min(max_tokens, all_tokens - done);

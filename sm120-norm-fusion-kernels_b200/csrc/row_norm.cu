@@ -51,39 +51,6 @@ struct RowArgs {
   float epsilon;
 };
 
-// s = round(x + r) for one pack (kAdd), returned packed; its square is added
-// to `acc` (a pair of accumulators: even and odd elements).
-template <typename T, bool kAdd>
-__device__ __forceinline__ uint4 combine(const uint4& x, const uint4& r, float2& acc) {
-  constexpr int kPairs = Pack<T>::kElems / 2;
-  float2 f[kPairs];
-  pack_to_pairs<T>(x, f);
-  uint4 s = x;
-  if constexpr (kAdd) {
-    float2 g[kPairs];
-    pack_to_pairs<T>(r, g);
-#pragma unroll
-    for (int i = 0; i < kPairs; ++i) f[i] = __fadd2_rn(f[i], g[i]);
-    s = pairs_to_pack<T>(f);
-    pack_to_pairs<T>(s, f);  // the rounded sum is what the oracle squares
-  }
-  acc = accumulate_square_pairs<T>(acc, f, kPairs);
-  return s;
-}
-
-// round(round32(s * inv) * w) for one pack.
-template <typename T>
-__device__ __forceinline__ uint4 scale(const uint4& s, const uint4& w, float inv) {
-  constexpr int kPairs = Pack<T>::kElems / 2;
-  const float2 inv2 = make_float2(inv, inv);
-  float2 f[kPairs], g[kPairs];
-  pack_to_pairs<T>(s, f);
-  pack_to_pairs<T>(w, g);
-#pragma unroll
-  for (int i = 0; i < kPairs; ++i) f[i] = __fmul2_rn(__fmul2_rn(f[i], inv2), g[i]);
-  return pairs_to_pack<T>(f);
-}
-
 // ---- warp family -----------------------------------------------------------
 template <typename T, bool kAdd, int kPacksPerLane>
 __global__ void __launch_bounds__(256) row_norm_warp_kernel(RowArgs<T> a) {
@@ -118,7 +85,7 @@ __global__ void __launch_bounds__(256) row_norm_warp_kernel(RowArgs<T> a) {
 #pragma unroll
     for (int i = 0; i < kPacksPerLane; ++i) {
       const int c = lane + i * kWarpSize;
-      if (c < packs) s[i] = combine<T, kAdd>(s[i], r[i], acc);
+      if (c < packs) s[i] = combine_pack<T, kAdd>(s[i], r[i], acc);
     }
     const float sum_sq = group_allreduce_sum<kWarpSize>(__fadd_rn(acc.x, acc.y));
     const float inv = inverse_rms(sum_sq, n, a.epsilon);
@@ -128,7 +95,7 @@ __global__ void __launch_bounds__(256) row_norm_warp_kernel(RowArgs<T> a) {
       if (c < packs) {
         const int64_t off = base + static_cast<int64_t>(c) * E;
         if constexpr (kAdd) store16(a.residual_output + off, s[i]);
-        store16(a.output + off, scale<T>(s[i], w[i], inv));
+        store16(a.output + off, normalise_pack<T>(s[i], w[i], inv));
       }
     }
   }
@@ -182,7 +149,7 @@ __global__ void __launch_bounds__(kMaxThreads) row_norm_cta_kernel(RowArgs<T> a)
 #pragma unroll
     for (int i = 0; i < kPacksPerThread; ++i) {
       const int c = threadIdx.x + i * blockDim.x;
-      if (c < packs) s[i] = combine<T, kAdd>(s[i], r[i], acc);
+      if (c < packs) s[i] = combine_pack<T, kAdd>(s[i], r[i], acc);
     }
     const float inv = inverse_rms(block_allreduce_sum(__fadd_rn(acc.x, acc.y), partial, parity),
                                   n, a.epsilon);
@@ -193,7 +160,7 @@ __global__ void __launch_bounds__(kMaxThreads) row_norm_cta_kernel(RowArgs<T> a)
       if (c < packs) {
         const int64_t off = base + static_cast<int64_t>(c) * E;
         if constexpr (kAdd) store16(a.residual_output + off, s[i]);
-        store16(a.output + off, scale<T>(s[i], w[i], inv));
+        store16(a.output + off, normalise_pack<T>(s[i], w[i], inv));
       }
     }
   }
@@ -216,7 +183,7 @@ __global__ void __launch_bounds__(1024) row_norm_wide_kernel(RowArgs<T> a) {
       const int64_t off = base + static_cast<int64_t>(c) * E;
       uint4 r;
       if constexpr (kAdd) r = load16(a.residual + off);
-      const uint4 s = combine<T, kAdd>(load16(a.input + off), r, acc);
+      const uint4 s = combine_pack<T, kAdd>(load16(a.input + off), r, acc);
       if constexpr (kAdd) store16(a.residual_output + off, s);
     }
     const float inv = inverse_rms(block_allreduce_sum(__fadd_rn(acc.x, acc.y), partial, parity),
@@ -227,7 +194,7 @@ __global__ void __launch_bounds__(1024) row_norm_wide_kernel(RowArgs<T> a) {
     for (int c = threadIdx.x; c < packs; c += blockDim.x) {
       const int64_t off = base + static_cast<int64_t>(c) * E;
       const uint4 s = load16(source + off);
-      store16(a.output + off, scale<T>(s, load16(a.weight + static_cast<int64_t>(c) * E), inv));
+      store16(a.output + off, normalise_pack<T>(s, load16(a.weight + static_cast<int64_t>(c) * E), inv));
     }
   }
 }
@@ -331,7 +298,7 @@ __global__ void __launch_bounds__(1024) row_norm_bulk_kernel(RowArgs<T> a, int s
       if (c < packs) {
         uint4 r;
         if constexpr (kAdd) r = load16_shared(stage + row_bytes + static_cast<uint32_t>(c) * 16);
-        v[k] = combine<T, kAdd>(load16_shared(stage + static_cast<uint32_t>(c) * 16), r, acc);
+        v[k] = combine_pack<T, kAdd>(load16_shared(stage + static_cast<uint32_t>(c) * 16), r, acc);
       }
     }
     const float sum_sq = group_allreduce_sum<kWarpSize>(__fadd_rn(acc.x, acc.y));
@@ -362,7 +329,7 @@ __global__ void __launch_bounds__(1024) row_norm_bulk_kernel(RowArgs<T> a, int s
       if (c < packs) {
         const int64_t off = base + static_cast<int64_t>(c) * E;
         if constexpr (kAdd) store16(a.residual_output + off, v[k]);
-        store16(a.output + off, scale<T>(v[k], w[k], inv));
+        store16(a.output + off, normalise_pack<T>(v[k], w[k], inv));
       }
     }
   }

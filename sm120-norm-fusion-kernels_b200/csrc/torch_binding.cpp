@@ -9,6 +9,12 @@
 //     CUDA implementations                                 (bindings.cpp:66-81)
 // Tensor validation raises RuntimeError with the reference's messages
 // (csrc/rmsnorm_kernels.cu:439-452, 488-492, 548-583, 624-676, 732-745).
+//
+// Beyond the reference: TORCH_LIBRARY(sm120_norm_ext) with the engine-side
+// extensions of the same path (generalised Q/K norm + RoPE + cache store;
+// RMSNorm with fp8 quantisation, under the operator names and argument order
+// fp8 inference engines use for those fusions). The reference's namespace is
+// left exactly as it is.
 // Everything else -- version checks, shape dispatch, launch -- happens behind
 // the C ABI in include/sm120norm_b200.h, on the tensors' device and on the
 // current PyTorch stream. No host synchronisation; only rms_norm and
@@ -235,6 +241,242 @@ TORCH_LIBRARY(sm120_norm, m) {
 TORCH_LIBRARY_IMPL(sm120_norm, CUDA, m) {
   m.impl("fused_qk_rms_norm_rope_", &b200_fused_qk_rms_norm_rope);
   m.impl("fused_qk_rms_norm_rope_kv_", &b200_fused_qk_rms_norm_rope_kv);
+}
+
+// ---------------------------------------------------------------------------
+// Extensions
+// ---------------------------------------------------------------------------
+namespace {
+
+bool is_fp8_storage(const torch::Tensor& t) {
+  return t.scalar_type() == torch::kFloat8_e4m3fn || t.scalar_type() == torch::kByte;
+}
+
+// [tokens, heads, head_dim] with adjacent heads and elements; any token stride.
+void check_head_rows(const torch::Tensor& t, const char* name) {
+  TORCH_CHECK(t.is_cuda(), name, " must be a CUDA tensor");
+  TORCH_CHECK(t.dim() == 3, name, " must have shape [tokens, heads, head_dim]");
+  TORCH_CHECK(t.size(2) <= 1 || t.stride(2) == 1, name, " must have unit element stride");
+  TORCH_CHECK(t.size(1) <= 1 || t.stride(1) == t.size(2), name,
+              " heads must be adjacent (head stride == head_dim)");
+}
+
+int64_t token_stride(const torch::Tensor& t) {
+  return t.size(0) <= 1 ? t.size(1) * t.size(2) : t.stride(0);
+}
+
+}  // namespace
+
+void b200_qk_norm_rope_cache(torch::Tensor query, torch::Tensor key,
+                             c10::optional<torch::Tensor> value, torch::Tensor query_weight,
+                             torch::Tensor key_weight, torch::Tensor positions,
+                             torch::Tensor cos_sin_cache, c10::optional<torch::Tensor> key_cache,
+                             c10::optional<torch::Tensor> value_cache,
+                             c10::optional<torch::Tensor> slot_mapping,
+                             c10::optional<torch::Tensor> k_scale,
+                             c10::optional<torch::Tensor> v_scale, bool is_neox,
+                             c10::string_view kv_cache_layout, double epsilon) {
+  check_head_rows(query, "query");
+  check_head_rows(key, "key");
+  TORCH_CHECK(query.size(0) == key.size(0), "query and key token counts must match");
+  TORCH_CHECK(query.size(2) == key.size(2), "query and key head sizes must match");
+  TORCH_CHECK(query.scalar_type() == key.scalar_type(), "query and key dtypes must match");
+  TORCH_CHECK(dtype_code(query) >= 0, "supported dtypes are float16, bfloat16, and float32");
+  const int64_t head_dim = query.size(2);
+  TORCH_CHECK(query_weight.is_cuda() && key_weight.is_cuda() && query_weight.is_contiguous() &&
+                  key_weight.is_contiguous(),
+              "Q/K weights must be contiguous CUDA tensors");
+  TORCH_CHECK(query_weight.numel() == head_dim && key_weight.numel() == head_dim,
+              "Q/K weights must contain head_dim elements");
+  TORCH_CHECK(query_weight.scalar_type() == query.scalar_type() &&
+                  key_weight.scalar_type() == query.scalar_type(),
+              "Q/K weight dtypes must match activations");
+  TORCH_CHECK(positions.is_cuda() && positions.is_contiguous() &&
+                  positions.scalar_type() == torch::kInt64 && positions.numel() == query.size(0),
+              "positions must be contiguous CUDA int64 with one entry per token");
+  TORCH_CHECK(cos_sin_cache.is_cuda() && cos_sin_cache.is_contiguous() &&
+                  cos_sin_cache.scalar_type() == torch::kFloat32 && cos_sin_cache.dim() >= 1,
+              "cos/sin cache must be a contiguous CUDA float32 tensor");
+  const int64_t rotary_dim = cos_sin_cache.size(-1);
+  const auto device = query.device();
+  TORCH_CHECK(key.device() == device && query_weight.device() == device &&
+                  key_weight.device() == device && positions.device() == device &&
+                  cos_sin_cache.device() == device,
+              "all tensors must be on the same CUDA device");
+
+  sm120n_qk_cache_args a{};
+  a.struct_size = sizeof(a);
+  a.dtype = dtype_code(query);
+  a.tokens = query.size(0);
+  a.query_heads = query.size(1);
+  a.key_heads = key.size(1);
+  a.head_dim = head_dim;
+  a.rotary_dim = rotary_dim;
+  a.rope_style = is_neox ? SM120N_ROPE_NEOX : SM120N_ROPE_INTERLEAVED;
+  a.cache_dtype = SM120N_CACHE_AUTO;
+  a.query = query.data_ptr();
+  a.query_token_stride = token_stride(query);
+  a.key = key.data_ptr();
+  a.key_token_stride = token_stride(key);
+  a.query_weight = query_weight.data_ptr();
+  a.key_weight = key_weight.data_ptr();
+  a.positions = positions.data_ptr<int64_t>();
+  a.cos_sin_cache = cos_sin_cache.data_ptr<float>();
+  a.rope_positions = rotary_dim == 0 ? 0 : cos_sin_cache.numel() / rotary_dim;
+  a.epsilon = static_cast<float>(epsilon);
+
+  const bool store = key_cache.has_value() || value_cache.has_value();
+  if (store) {
+    TORCH_CHECK(key_cache.has_value() && value_cache.has_value() && value.has_value() &&
+                    slot_mapping.has_value(),
+                "a KV store needs value, key_cache, value_cache and slot_mapping");
+    const auto& v = *value;
+    const auto& kc = *key_cache;
+    const auto& vc = *value_cache;
+    const auto& slots = *slot_mapping;
+    check_head_rows(v, "value");
+    TORCH_CHECK(v.sizes() == key.sizes() && v.scalar_type() == key.scalar_type(),
+                "value shape and dtype must match key");
+    const bool nhd = kv_cache_layout == "NHD";
+    TORCH_CHECK(nhd || kv_cache_layout == "HND", "kv_cache_layout must be \"NHD\" or \"HND\"");
+    TORCH_CHECK(kc.is_cuda() && vc.is_cuda() && kc.dim() == 4 && vc.sizes() == kc.sizes() &&
+                    vc.strides() == kc.strides() && vc.scalar_type() == kc.scalar_type(),
+                "key_cache and value_cache must be 4-D CUDA tensors of one shape, stride "
+                "and dtype");
+    const int64_t head_axis = nhd ? 2 : 1;
+    const int64_t slot_axis = nhd ? 1 : 2;
+    TORCH_CHECK(kc.size(head_axis) == key.size(1) && kc.size(3) == head_dim,
+                nhd ? "NHD caches must be [blocks, block_size, key_heads, head_dim]"
+                    : "HND caches must be [blocks, key_heads, block_size, head_dim]");
+    TORCH_CHECK(kc.stride(3) == 1, "KV caches must have unit element stride");
+    const bool fp8 = is_fp8_storage(kc);
+    TORCH_CHECK(fp8 || kc.scalar_type() == query.scalar_type(),
+                "KV caches must use the activation dtype or fp8 e4m3 (float8_e4m3fn / uint8)");
+    TORCH_CHECK(slots.is_cuda() && slots.is_contiguous() && slots.scalar_type() == torch::kInt &&
+                    slots.numel() == query.size(0),
+                "slot_mapping must be contiguous CUDA int32 with one entry per token");
+    TORCH_CHECK(v.device() == device && kc.device() == device && vc.device() == device &&
+                    slots.device() == device,
+                "all tensors must be on the same CUDA device");
+    if (fp8) {
+      TORCH_CHECK(k_scale.has_value() && v_scale.has_value(), "fp8 caches need k_scale and v_scale");
+      for (const auto* scale : {&*k_scale, &*v_scale}) {
+        TORCH_CHECK(scale->is_cuda() && scale->scalar_type() == torch::kFloat32 &&
+                        scale->numel() == 1 && scale->device() == device,
+                    "k_scale and v_scale must be one-element CUDA float32 tensors");
+      }
+      a.cache_dtype = SM120N_CACHE_FP8_E4M3;
+      a.k_scale = k_scale->data_ptr<float>();
+      a.v_scale = v_scale->data_ptr<float>();
+    }
+    a.value = v.data_ptr();
+    a.value_token_stride = token_stride(v);
+    a.key_cache = kc.data_ptr();
+    a.value_cache = vc.data_ptr();
+    a.slot_mapping = slots.data_ptr<int32_t>();
+    a.num_blocks = kc.size(0);
+    a.block_size = kc.size(slot_axis);
+    a.cache_block_stride = kc.stride(0);
+    a.cache_slot_stride = kc.stride(slot_axis);
+    a.cache_head_stride = kc.stride(head_axis);
+  }
+  c10::cuda::CUDAGuard guard(device);
+  raise_if_failed(sm120n_qk_norm_rope_cache(&a, current_stream()));
+}
+
+namespace {
+
+void check_quant_output(const torch::Tensor& result, const torch::Tensor& input) {
+  TORCH_CHECK(result.is_cuda() && result.is_contiguous() && is_fp8_storage(result),
+              "result must be a contiguous CUDA float8_e4m3fn (or uint8) tensor");
+  TORCH_CHECK(result.sizes() == input.sizes(), "result shape must match input");
+  TORCH_CHECK(result.device() == input.device(), "all tensors must be on the same CUDA device");
+}
+
+void check_scalar_scale(const torch::Tensor& scale, const torch::Tensor& input, const char* name) {
+  TORCH_CHECK(scale.is_cuda() && scale.scalar_type() == torch::kFloat32 && scale.numel() == 1 &&
+                  scale.device() == input.device(),
+              name, " must be a one-element CUDA float32 tensor");
+}
+
+void run_norm_quant(torch::Tensor& result, const torch::Tensor& input,
+                    const c10::optional<torch::Tensor>& residual, const torch::Tensor& weight,
+                    const float* scale, float* token_scales, const float* scale_ub,
+                    double epsilon) {
+  check_activation_and_weight(input, weight);
+  check_quant_output(result, input);
+  const void* residual_ptr = nullptr;
+  if (residual.has_value()) {
+    check_like_input(*residual, input, "residual");
+    residual_ptr = residual->data_ptr();
+  }
+  c10::cuda::CUDAGuard guard(input.device());
+  const int64_t hidden = input.size(-1);
+  const int64_t rows = hidden == 0 ? 0 : input.numel() / hidden;
+  raise_if_failed(sm120n_rms_norm_fp8_quant(
+      input.data_ptr(), residual_ptr, weight.data_ptr(), const_cast<void*>(residual_ptr),
+      result.data_ptr(), scale, token_scales, scale_ub, rows, hidden, dtype_code(input),
+      static_cast<float>(epsilon), current_stream()));
+}
+
+}  // namespace
+
+void b200_rms_norm_static_fp8_quant(torch::Tensor result, torch::Tensor input,
+                                    torch::Tensor weight, torch::Tensor scale, double epsilon) {
+  check_scalar_scale(scale, input, "scale");
+  run_norm_quant(result, input, c10::nullopt, weight, scale.data_ptr<float>(), nullptr, nullptr,
+                 epsilon);
+}
+
+// residual = input + residual (in place); result = quant(RMSNorm(residual)).
+void b200_fused_add_rms_norm_static_fp8_quant(torch::Tensor result, torch::Tensor input,
+                                              torch::Tensor residual, torch::Tensor weight,
+                                              torch::Tensor scale, double epsilon) {
+  check_scalar_scale(scale, input, "scale");
+  run_norm_quant(result, input, residual, weight, scale.data_ptr<float>(), nullptr, nullptr,
+                 epsilon);
+}
+
+void b200_rms_norm_dynamic_per_token_quant(torch::Tensor result, torch::Tensor input,
+                                           torch::Tensor weight, torch::Tensor scale,
+                                           double epsilon, c10::optional<torch::Tensor> scale_ub,
+                                           c10::optional<torch::Tensor> residual) {
+  const int64_t hidden = input.size(-1);
+  const int64_t rows = hidden == 0 ? 0 : input.numel() / hidden;
+  TORCH_CHECK(scale.is_cuda() && scale.is_contiguous() && scale.scalar_type() == torch::kFloat32 &&
+                  scale.numel() == rows && scale.device() == input.device(),
+              "scale must be a contiguous CUDA float32 tensor with one entry per row");
+  const float* ub = nullptr;
+  if (scale_ub.has_value()) {
+    check_scalar_scale(*scale_ub, input, "scale_ub");
+    ub = scale_ub->data_ptr<float>();
+  }
+  run_norm_quant(result, input, residual, weight, nullptr, scale.data_ptr<float>(), ub, epsilon);
+}
+
+TORCH_LIBRARY(sm120_norm_ext, m) {
+  m.def(
+      "qk_norm_rope_cache_(Tensor(a!) query, Tensor(b!) key, Tensor? value, "
+      "Tensor query_weight, Tensor key_weight, Tensor positions, Tensor cos_sin_cache, "
+      "Tensor(c!)? key_cache, Tensor(d!)? value_cache, Tensor? slot_mapping, "
+      "Tensor? k_scale, Tensor? v_scale, bool is_neox=True, str kv_cache_layout=\"NHD\", "
+      "float epsilon=1e-6) -> ()");
+  m.def(
+      "rms_norm_static_fp8_quant(Tensor(a!) result, Tensor input, Tensor weight, "
+      "Tensor scale, float epsilon) -> ()");
+  m.def(
+      "fused_add_rms_norm_static_fp8_quant(Tensor(a!) result, Tensor input, "
+      "Tensor(b!) residual, Tensor weight, Tensor scale, float epsilon) -> ()");
+  m.def(
+      "rms_norm_dynamic_per_token_quant(Tensor(a!) result, Tensor input, Tensor weight, "
+      "Tensor(b!) scale, float epsilon, Tensor? scale_ub, Tensor(c!)? residual) -> ()");
+}
+
+TORCH_LIBRARY_IMPL(sm120_norm_ext, CUDA, m) {
+  m.impl("qk_norm_rope_cache_", &b200_qk_norm_rope_cache);
+  m.impl("rms_norm_static_fp8_quant", &b200_rms_norm_static_fp8_quant);
+  m.impl("fused_add_rms_norm_static_fp8_quant", &b200_fused_add_rms_norm_static_fp8_quant);
+  m.impl("rms_norm_dynamic_per_token_quant", &b200_rms_norm_dynamic_per_token_quant);
 }
 
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {

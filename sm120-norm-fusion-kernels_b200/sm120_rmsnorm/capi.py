@@ -17,6 +17,51 @@ LIBRARY_PATH = Path(__file__).resolve().parent / LIBRARY_NAME
 
 F32, F16, BF16 = 0, 1, 2
 OK, ERR_INVALID_ARGUMENT, ERR_UNSUPPORTED, ERR_CUDA = 0, 1, 2, 3
+ROPE_NEOX, ROPE_INTERLEAVED = 0, 1
+CACHE_AUTO, CACHE_FP8_E4M3 = 0, 1
+
+
+class QkCacheArgs(ctypes.Structure):
+    """``sm120n_qk_cache_args`` (include/sm120norm_b200.h), field for field."""
+
+    _fields_ = [
+        ("struct_size", ctypes.c_uint32),
+        ("dtype", ctypes.c_int32),
+        ("tokens", ctypes.c_int64),
+        ("query_heads", ctypes.c_int64),
+        ("key_heads", ctypes.c_int64),
+        ("head_dim", ctypes.c_int64),
+        ("rotary_dim", ctypes.c_int64),
+        ("rope_style", ctypes.c_int32),
+        ("cache_dtype", ctypes.c_int32),
+        ("query", ctypes.c_void_p),
+        ("query_token_stride", ctypes.c_int64),
+        ("key", ctypes.c_void_p),
+        ("key_token_stride", ctypes.c_int64),
+        ("value", ctypes.c_void_p),
+        ("value_token_stride", ctypes.c_int64),
+        ("query_weight", ctypes.c_void_p),
+        ("key_weight", ctypes.c_void_p),
+        ("positions", ctypes.c_void_p),
+        ("cos_sin_cache", ctypes.c_void_p),
+        ("rope_positions", ctypes.c_int64),
+        ("key_cache", ctypes.c_void_p),
+        ("value_cache", ctypes.c_void_p),
+        ("slot_mapping", ctypes.c_void_p),
+        ("num_blocks", ctypes.c_int64),
+        ("block_size", ctypes.c_int64),
+        ("cache_block_stride", ctypes.c_int64),
+        ("cache_slot_stride", ctypes.c_int64),
+        ("cache_head_stride", ctypes.c_int64),
+        ("k_scale", ctypes.c_void_p),
+        ("v_scale", ctypes.c_void_p),
+        ("epsilon", ctypes.c_float),
+    ]
+
+    def __init__(self, **fields):
+        fields.setdefault("epsilon", 1e-6)
+        super().__init__(struct_size=ctypes.sizeof(QkCacheArgs), **fields)
+
 
 # Every symbol include/sm120norm_b200.h declares, with its ctypes signature.
 _i64, _i32, _f32, _vp = ctypes.c_int64, ctypes.c_int, ctypes.c_float, ctypes.c_void_p
@@ -35,6 +80,9 @@ SIGNATURES: dict[str, tuple[list, object]] = {
     "sm120n_fused_qk_rms_norm_rope_kv": (
         [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp,
          _i64, _i64, _i64, _i64, _i64, _i64, _i32, _f32, _i32, _vp], _i32),
+    "sm120n_qk_norm_rope_cache": ([ctypes.POINTER(QkCacheArgs), _vp], _i32),
+    "sm120n_rms_norm_fp8_quant": (
+        [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _i64, _i64, _i32, _f32, _vp], _i32),
 }
 
 
@@ -115,3 +163,18 @@ def fused_qk_rms_norm_rope_kv(query_ptr, key_ptr, value_ptr, query_weight_ptr, k
         query_ptr, key_ptr, value_ptr, query_weight_ptr, key_weight_ptr, positions_ptr,
         cos_sin_ptr, key_cache_ptr, value_cache_ptr, slot_mapping_ptr, tokens, query_heads,
         key_heads, head_dim, rope_positions, cache_slots, dtype, epsilon, version, stream))
+
+
+def qk_norm_rope_cache(args: QkCacheArgs, stream=0) -> None:
+    """Generalised Q/K norm + RoPE + cache store (sm120n_qk_norm_rope_cache)."""
+    _check(load().sm120n_qk_norm_rope_cache(ctypes.byref(args), stream))
+
+
+def rms_norm_fp8_quant(input_ptr, residual_ptr, weight_ptr, residual_output_ptr, output_ptr,
+                       scale_ptr, token_scales_ptr, scale_ub_ptr, rows, hidden_size, dtype,
+                       epsilon=1e-6, stream=0) -> None:
+    """RMSNorm (+ residual add) with fp8 e4m3 output; pass 0 / None for absent
+    pointers (sm120n_rms_norm_fp8_quant)."""
+    _check(load().sm120n_rms_norm_fp8_quant(
+        input_ptr, residual_ptr, weight_ptr, residual_output_ptr, output_ptr, scale_ptr,
+        token_scales_ptr, scale_ub_ptr, rows, hidden_size, dtype, epsilon, stream))

@@ -87,16 +87,19 @@ def assert_bitwise_equal(actual: torch.Tensor, expected: torch.Tensor, what: str
 
 def rope_bound(x: torch.Tensor, weight: torch.Tensor, positions: torch.Tensor,
                cos_sin: torch.Tensor, expected: torch.Tensor, k: int | None = None,
-               eps: float = 1e-6) -> torch.Tensor:
+               eps: float = 1e-6, interleaved: bool = False) -> torch.Tensor:
     """Propagation part of the RoPE tolerance for a [T, H, D] head tensor
     (module docstring): |dn_i||c_i| + |dn_j||s_i| with
     |dn| = k * (ulp(t)|w| + ulp(n)), t and n evaluated in fp64 from the inputs.
-    assert_rope_close / rope_violations add k ulp of the output."""
+    The rotary width R is cos_sin's last dimension (R <= D); elements beyond R
+    are not rotated and get |dn|. Partners are (i, i + R/2), or (2i, 2i + 1)
+    when `interleaved`. assert_rope_close / rope_violations add k ulp of the
+    output."""
     dtype = expected.dtype
     k = default_rope_k(dtype) if k is None else k
     xd = x.detach().cpu().to(torch.float64)
-    d = xd.shape[-1]
-    half = d // 2
+    rotary = cos_sin.shape[-1]
+    half = rotary // 2
     w = weight.detach().cpu().to(torch.float64)
     t = xd * torch.rsqrt(xd.square().mean(-1, keepdim=True) + eps)
     n = t * w
@@ -105,10 +108,16 @@ def rope_bound(x: torch.Tensor, weight: torch.Tensor, positions: torch.Tensor,
         return torch.maximum(ulp_at(v, dtype), ulp_at(v.to(dtype).to(torch.float64), dtype))
 
     dn = k * (ulp_rounded(t) * w.abs() + ulp_rounded(n))
-    rows = cos_sin.detach().cpu().reshape(-1, d).to(torch.float64)[positions.cpu().long()]
+    rows = cos_sin.detach().cpu().reshape(-1, rotary).to(torch.float64)[positions.cpu().long()]
     c, s = rows[:, None, :half].abs(), rows[:, None, half:].abs()
-    d1, d2 = dn[..., :half], dn[..., half:]
-    return torch.cat((d1 * c + d2 * s, d2 * c + d1 * s), dim=-1)
+    rot = dn[..., :rotary]
+    if interleaved:
+        d1, d2 = rot[..., 0::2], rot[..., 1::2]
+        bound = torch.stack((d1 * c + d2 * s, d2 * c + d1 * s), dim=-1).flatten(-2)
+    else:
+        d1, d2 = rot[..., :half], rot[..., half:]
+        bound = torch.cat((d1 * c + d2 * s, d2 * c + d1 * s), dim=-1)
+    return torch.cat((bound, dn[..., rotary:]), dim=-1)
 
 
 def default_rope_k(dtype: torch.dtype) -> int:
