@@ -420,6 +420,7 @@ def _measure_rest(args, dist, ops, flush, data, step_ms, launches_per_step) -> d
 
     per_op = {} if args.skip_per_op else per_op_suite(ops, flush, dist, args)
     extensions = {} if args.skip_per_op else extension_suite(flush, dist, args)
+    engine = {} if args.skip_per_op else engine_suite(flush, dist, args)
 
     return {
         "metric": "achieved HBM GB/s (% of B200 peak) and us/call per op at 1/2/4/8 GPUs",
@@ -436,7 +437,7 @@ def _measure_rest(args, dist, ops, flush, data, step_ms, launches_per_step) -> d
                    "l2": "flushed (512 MiB write) before every timed step and every "
                          "per-launch timing, outside the events"},
         "roofline": roofline, "e2e": e2e, "gpu_launches": launches_per_step * args.steps,
-        "per_shape": per_shape, "per_op": per_op, "extensions": extensions,
+        "per_shape": per_shape, "per_op": per_op, "extensions": extensions, "engine": engine,
         "device": torch.cuda.get_device_name(dev),
     }
 
@@ -714,6 +715,118 @@ def extension_suite(flush: Flusher, dist: Dist, args) -> dict:
                    nbytes, comparator=True)
             del sets
     out["vllm_comparator"] = "loaded" if vllm is not None else "unavailable"
+    return out
+
+
+def engine_suite(flush: Flusher, dist: Dist, args) -> dict:
+    """Decode-step attention prologues of a Qwen3-8B-shaped model (hidden 4096,
+    32 query / 8 KV heads of 128, bf16, random weights): for each of L layers
+    residual add + input RMSNorm, the QKV projection (cuBLAS through PyTorch),
+    Q/K norm + RoPE + paged KV store; L layers captured in one CUDA graph per
+    path and batch, replayed after an L2 flush. Paths: this package
+    (sm120_rmsnorm.engine.DecodeGraph: 2 own kernels per layer, in place on the
+    QKV buffer), the reference's kernels (contiguous Q / K / V copies first,
+    as its operator requires), and vLLM's kernels when they load. `gemm_only`
+    is the projection plus the stand-in copy between layers, so
+    `norm_us_per_layer` = (path - gemm_only) / L is the per-layer cost of the
+    normalisation path itself."""
+    from oracle import build_ref
+    from sm120_rmsnorm.engine import (DecodeGraph, Qwen3AttentionPrologue, Qwen3AttentionShape,
+                                      rope_cos_sin_cache)
+
+    shape = Qwen3AttentionShape()
+    n_layers = 8
+    reps = max(3, args.reps)
+    bf = torch.bfloat16
+    g = torch.Generator(device="cuda").manual_seed(31 + dist.rank)
+    cpu_g = torch.Generator().manual_seed(37 + dist.rank)
+    layers = [Qwen3AttentionPrologue(shape, "cuda", generator=g) for _ in range(n_layers)]
+    cos_sin = rope_cos_sin_cache(shape, "cuda")
+    cos_bf = cos_sin.to(bf)
+    ref = build_ref.load()
+    vllm = vllm_ops()
+    one = torch.ones(1, device="cuda")
+    out = {"model": "Qwen3-8B-shaped attention prologue (hidden 4096, 32/8 heads x 128, bf16)",
+           "layers": n_layers}
+
+    def time_graph_us(graph):
+        return dist.max(time_graph(graph, flush, reps))
+
+    def generic_graph(batch, positions, slots, kcs, vcs, prologue):
+        hidden = torch.randn(batch, shape.hidden, device="cuda", generator=g).to(bf)
+        residual = torch.randn(batch, shape.hidden, device="cuda", generator=g).to(bf)
+        qkvs = [torch.empty(batch, shape.qkv_width, device="cuda", dtype=bf) for _ in layers]
+        nexts = [torch.empty_like(hidden) for _ in layers[1:]]
+
+        def run():
+            h = hidden
+            for i, layer in enumerate(layers):
+                prologue(layer, h, residual, positions, slots, kcs[i], vcs[i], qkvs[i])
+                if i + 1 < len(layers):
+                    nexts[i].copy_(qkvs[i][:, :shape.hidden])
+                    h = nexts[i]
+        graph, _ = capture([run])
+        return graph
+
+    def gemm_only(layer, h, r, pos, slots, kc, vc, qkv):
+        torch.matmul(h, layer.qkv_weight.t(), out=qkv)
+
+    def reference_path(layer, h, r, pos, slots, kc, vc, qkv):
+        ref.fused_add_rms_norm_inplace(h, r, layer.input_norm_weight, EPS, 0)
+        torch.matmul(h, layer.qkv_weight.t(), out=qkv)
+        q, k, v = (t.contiguous() for t in layer.split(qkv))
+        ref.fused_qk_rms_norm_rope_kv(q, k, v, layer.query_norm_weight, layer.key_norm_weight,
+                                      pos, cos_sin, kc, vc, slots, EPS, 1)
+
+    def vllm_path(layer, h, r, pos, slots, kc, vc, qkv):
+        C, cache_ops = vllm
+        C.fused_add_rms_norm(h, r, layer.input_norm_weight, EPS)
+        torch.matmul(h, layer.qkv_weight.t(), out=qkv)
+        C.fused_qk_norm_rope(qkv, shape.query_heads, shape.key_heads, shape.key_heads,
+                             shape.head_dim, EPS, layer.query_norm_weight, layer.key_norm_weight,
+                             cos_bf, True, pos)
+        _, k, v = layer.split(qkv)
+        cache_ops.reshape_and_cache_flash(k, v, kc, vc, slots.long(), "auto", one, one)
+
+    for batch in (1, 64, 256):
+        blocks = max(64, 4 * batch // 16)
+        kcs = [torch.zeros(blocks, 16, shape.key_heads, shape.head_dim, device="cuda", dtype=bf)
+               for _ in layers]
+        vcs = [torch.zeros_like(kc) for kc in kcs]
+        positions = torch.randperm(shape.max_positions, generator=cpu_g)[:batch].cuda()
+        slots = torch.randperm(blocks * 16, generator=cpu_g)[:batch].to(torch.int32).cuda()
+        row = {}
+        ours = DecodeGraph(layers, batch, cos_sin, kcs, vcs)
+        ours.hidden.copy_(torch.randn(batch, shape.hidden, device="cuda", generator=g).to(bf))
+        ours.residual.copy_(torch.randn(batch, shape.hidden, device="cuda", generator=g).to(bf))
+        ours.positions.copy_(positions)
+        ours.slot_mapping.copy_(slots)
+        row["b200"] = time_graph_us(ours.graph)
+        del ours
+        base = generic_graph(batch, positions, slots, kcs, vcs, gemm_only)
+        row["gemm_only"] = time_graph_us(base)
+        del base
+        if ref is not None:
+            graph = generic_graph(batch, positions, slots, kcs, vcs, reference_path)
+            row["reference_kernels"] = time_graph_us(graph)
+            del graph
+        if vllm is not None:
+            try:
+                graph = generic_graph(batch, positions, slots, kcs, vcs, vllm_path)
+                row["vllm"] = time_graph_us(graph)
+                del graph
+            except Exception as e:  # noqa: BLE001 - a comparator may be unavailable
+                row["vllm_unavailable"] = f"{type(e).__name__}: {str(e)[:160]}"
+                torch.cuda.synchronize()
+        entry = {"us_per_step": {k: round(v, 2) for k, v in row.items()
+                                 if isinstance(v, float)}}
+        entry["norm_us_per_layer"] = {
+            k: round((v - row["gemm_only"]) / n_layers, 3) for k, v in row.items()
+            if isinstance(v, float) and k != "gemm_only"}
+        if "vllm_unavailable" in row:
+            entry["vllm_unavailable"] = row["vllm_unavailable"]
+        out[f"decode B={batch}"] = entry
+        del kcs, vcs
     return out
 
 

@@ -111,7 +111,7 @@ __device__ __forceinline__ void store_fp8_chunk(uint8_t* p, uint2 v) {
 }
 
 template <typename T, int D, int kCache, bool kVector>
-__global__ void __launch_bounds__(256, sizeof(T) == 2 ? 4 : 2) head_cache_kernel(CacheArgs<T> a) {
+__global__ void __launch_bounds__(256, sizeof(T) == 2 ? 5 : 2) head_cache_kernel(CacheArgs<T> a) {
   constexpr int kLanes = D / (2 * kChunkElems);
   constexpr int kHeadsPerWarp = kWarpSize / kLanes;
   wait_for_upstream_grid();

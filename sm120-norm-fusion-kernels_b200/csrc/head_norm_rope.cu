@@ -73,8 +73,14 @@ struct HeadJob {
   bool active;
 };
 
-template <typename T, bool kStoreKV, bool kVector>
-__global__ void __launch_bounds__(256, sizeof(T) == 2 ? 4 : 2) head_norm_rope_kernel(HeadArgs<T> a) {
+// kHoistWeights: each lane keeps its chunks of both weights in registers for
+// the whole launch (lowest latency: batch-1 decode); otherwise it loads the
+// selected weight per head from L1, which frees 16 registers for a fifth
+// resident block per SM and more loads in flight (measured on B200 for the
+// 32768-token prefill: 244 us against 256 us).
+template <typename T, bool kStoreKV, bool kVector, bool kHoistWeights>
+__global__ void __launch_bounds__(256, sizeof(T) == 2 ? (kHoistWeights ? 4 : 5) : 2)
+    head_norm_rope_kernel(HeadArgs<T> a) {
   wait_for_upstream_grid();
   release_downstream_grid();
   const int lane = threadIdx.x & (kWarpSize - 1);
@@ -89,10 +95,13 @@ __global__ void __launch_bounds__(256, sizeof(T) == 2 ? 4 : 2) head_norm_rope_ke
   const uint32_t warp = (blockIdx.x * blockDim.x + threadIdx.x) / kWarpSize;
   const uint32_t warps = (gridDim.x * blockDim.x) / kWarpSize;
 
-  const Half8<T> qw_lo = load_half<T, kVector>(a.query_weight + lo);
-  const Half8<T> qw_hi = load_half<T, kVector>(a.query_weight + hi);
-  const Half8<T> kw_lo = load_half<T, kVector>(a.key_weight + lo);
-  const Half8<T> kw_hi = load_half<T, kVector>(a.key_weight + hi);
+  Half8<T> qw_lo{}, qw_hi{}, kw_lo{}, kw_hi{};
+  if constexpr (kHoistWeights) {
+    qw_lo = load_half<T, kVector>(a.query_weight + lo);
+    qw_hi = load_half<T, kVector>(a.query_weight + hi);
+    kw_lo = load_half<T, kVector>(a.key_weight + lo);
+    kw_hi = load_half<T, kVector>(a.key_weight + hi);
+  }
 
   auto begin = [&](HeadJob<T>& job, uint32_t unit) {
     job.active = unit < units;
@@ -133,10 +142,17 @@ __global__ void __launch_bounds__(256, sizeof(T) == 2 ? 4 : 2) head_norm_rope_ke
     const float total = group_allreduce_sum<kLanesPerHead>(lane_sum);  // all lanes, before any exit
     if (!job.active || job.position < 0 || job.position >= a.rope_positions) return;
     const float inv = head_inverse_rms<kHeadDim>(make_float2(total, 0.0f), a.epsilon);
-    const Half8<T> n_lo =
-        normalise_half<T>(job.x_lo, select_half<T>(job.is_query, qw_lo, kw_lo), inv);
-    const Half8<T> n_hi =
-        normalise_half<T>(job.x_hi, select_half<T>(job.is_query, qw_hi, kw_hi), inv);
+    Half8<T> w_lo, w_hi;
+    if constexpr (kHoistWeights) {
+      w_lo = select_half<T>(job.is_query, qw_lo, kw_lo);
+      w_hi = select_half<T>(job.is_query, qw_hi, kw_hi);
+    } else {
+      const T* weight = job.is_query ? a.query_weight : a.key_weight;
+      w_lo = load_half<T, kVector>(weight + lo);
+      w_hi = load_half<T, kVector>(weight + hi);
+    }
+    const Half8<T> n_lo = normalise_half<T>(job.x_lo, w_lo, inv);
+    const Half8<T> n_hi = normalise_half<T>(job.x_hi, w_hi, inv);
     float2 c[4], sn[4];
     load8_pairs<kVector>(a.cos_sin + job.position * kHeadDim + lo, c);
     load8_pairs<kVector>(a.cos_sin + job.position * kHeadDim + hi, sn);
@@ -174,8 +190,14 @@ int run_heads(HeadArgs<T> a, int threads_per_block, cudaStream_t stream) {
   DeviceInfo dev;
   int rc = current_device_info(&dev);
   if (rc != SM120N_OK) return rc;
-  auto kernel = vector ? head_norm_rope_kernel<T, kStoreKV, true>
-                       : head_norm_rope_kernel<T, kStoreKV, false>;
+  // Below about 2048 heads per launch (decode batches up to ~64) the launch is
+  // latency-bound and the hoisted-weight form is faster (batch-1 decode:
+  // 2.37 us against 2.48 us); above, occupancy wins.
+  const bool hoist = a.tokens * (a.query_heads + a.key_heads) < 2048;
+  auto kernel = vector ? (hoist ? head_norm_rope_kernel<T, kStoreKV, true, true>
+                                : head_norm_rope_kernel<T, kStoreKV, true, false>)
+                       : (hoist ? head_norm_rope_kernel<T, kStoreKV, false, true>
+                                : head_norm_rope_kernel<T, kStoreKV, false, false>);
   const int64_t heads_per_warp = kHeadsPerWarp;
   // Keep tokens * heads below 2^31 per launch (the kernel indexes units in
   // 32 bits); larger calls become consecutive launches on the same stream.

@@ -270,13 +270,21 @@ int grid_for(Kernel kernel, int threads, int64_t rows, int* grid) {
   return SM120N_OK;
 }
 
+// `one_row_per_block`: a block per row, balanced by the block scheduler (the
+// better shape for many wide rows, as for the plain row kernels); otherwise a
+// persistent grid with a row loop.
 template <typename T, bool kAdd, bool kDynamic, int kPPT, int kMaxThreads>
-int launch_quant_cta(const QuantArgs<T>& a, int packs, cudaStream_t stream) {
+int launch_quant_cta(const QuantArgs<T>& a, int packs, cudaStream_t stream,
+                     bool one_row_per_block = false) {
   auto kernel = norm_quant_cta_kernel<T, kAdd, kDynamic, kPPT, kMaxThreads>;
   const int threads = (((packs + kPPT - 1) / kPPT) + kWarpSize - 1) / kWarpSize * kWarpSize;
   int grid = 0;
-  int rc = grid_for(kernel, threads, a.rows, &grid);
-  if (rc != SM120N_OK) return rc;
+  if (one_row_per_block && a.rows <= INT32_MAX) {
+    grid = static_cast<int>(a.rows);
+  } else {
+    int rc = grid_for(kernel, threads, a.rows, &grid);
+    if (rc != SM120N_OK) return rc;
+  }
   return launch(kernel, dim3(grid), dim3(threads), 0, stream, a);
 }
 
@@ -290,7 +298,19 @@ int run_quant(const QuantArgs<T>& a, cudaStream_t stream) {
   // At most 512 threads per block, so a thread may hold its packs of x, r
   // and w in up to 128 registers without spilling.
   if (vectorisable && packs <= 4 * 512) {
+    // Chosen from measurements on B200 (graphs of back-to-back calls on cold
+    // data): rows wider than 512 packs with many rows run best as persistent
+    // 256-thread blocks holding four packs per thread (65536 x 8192 bf16 with
+    // the residual add: 569 us against 607 us with 512 threads of two packs);
+    // narrower or fewer rows keep two packs per thread.
+    DeviceInfo dev;
+    int rc = current_device_info(&dev);
+    if (rc != SM120N_OK) return rc;
+    const bool many_rows = a.rows >= 8 * static_cast<int64_t>(dev.sm_count);
     if (packs <= 256) return launch_quant_cta<T, kAdd, kDynamic, 1, 256>(a, packs, stream);
+    if (many_rows && packs > 512 && packs <= 1024) {
+      return launch_quant_cta<T, kAdd, kDynamic, 4, 256>(a, packs, stream);
+    }
     if (packs <= 1024) return launch_quant_cta<T, kAdd, kDynamic, 2, 512>(a, packs, stream);
     return launch_quant_cta<T, kAdd, kDynamic, 4, 512>(a, packs, stream);
   }

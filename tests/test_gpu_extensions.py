@@ -310,6 +310,27 @@ def test_norm_quant_exact(dtype, hidden, add, dynamic):
         assert_bitwise_equal(r_out, want_r, what="residual")
 
 
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
+@pytest.mark.parametrize("add", [False, True])
+@pytest.mark.parametrize("dynamic", [False, True])
+def test_norm_quant_many_wide_rows_exact(dtype, add, dynamic):
+    """1200 rows of 8192: more than eight rows per SM, the persistent
+    four-packs-per-thread launch."""
+    g = gen(8192 + add + 2 * dynamic)
+    limit = 8 if add else 16
+    x = exact_values((1200, 8192), dtype, g, limit)
+    r = exact_values((1200, 8192), dtype, g, limit) if add else None
+    w = weights(8192, dtype, g)
+    scale = None if dynamic else torch.tensor([0.03])
+    q, scales, r_out = run_quant(x, w, r, scale)
+    want_q, want_scales, want_r = ex.rms_norm_fp8_quant(x, w, residual=r, scale=scale)
+    assert torch.equal(q.view(torch.uint8), want_q.view(torch.uint8))
+    if dynamic:
+        assert_bitwise_equal(scales, want_scales.reshape(-1), what="token scales")
+    if add:
+        assert_bitwise_equal(r_out, want_r, what="residual")
+
+
 @pytest.mark.parametrize("dtype", DTYPES)
 @pytest.mark.parametrize("hidden", [1024, 4096, 32768])
 @pytest.mark.parametrize("dynamic", [False, True])
