@@ -994,6 +994,32 @@ def profile_case(args) -> None:
             fn = lambda: ops.fused_add_rms_norm_inplace(x, r, w, EPS, args.version)
         else:
             fn = lambda: ops.rms_norm_out(x, w, y, EPS, args.version or 2)
+    elif args.profile == "quant":
+        from sm120_rmsnorm import extensions as ext
+        x = torch.randn(t, h, device="cuda", generator=g).to(dt)
+        r = torch.randn(t, h, device="cuda", generator=g).to(dt)
+        w = (1 + 0.1 * torch.randn(h, device="cuda", generator=g)).to(dt)
+        out = torch.empty(t, h, device="cuda", dtype=torch.float8_e4m3fn)
+        scale = torch.full((1,), 0.05, device="cuda")
+        fn = lambda: ext.fused_add_rms_norm_static_fp8_quant(out, x, r, w, scale, EPS)
+    elif args.profile == "qkcache":
+        from sm120_rmsnorm import extensions as ext
+        hq, hk = (int(v) for v in args.heads.split(","))
+        qkv = torch.randn(t, (hq + 2 * hk) * 128, device="cuda", generator=g).to(dt)
+        q = qkv[:, :hq * 128].view(t, hq, 128)
+        k = qkv[:, hq * 128:(hq + hk) * 128].view(t, hk, 128)
+        v = qkv[:, (hq + hk) * 128:].view(t, hk, 128)
+        qw = (1 + 0.1 * torch.randn(128, device="cuda", generator=g)).to(dt)
+        inv = 1.0 / (1e6 ** (torch.arange(0, 128, 2, dtype=torch.float32, device="cuda") / 128))
+        f = torch.outer(torch.arange(32768, dtype=torch.float32, device="cuda"), inv)
+        cache = torch.cat((f.cos(), f.sin()), dim=-1)
+        pos = torch.randint(0, 32768, (t,), device="cuda")
+        blocks = max(t, 2048 * 16) // 16
+        kc = torch.zeros(blocks, 16, hk, 128, device="cuda", dtype=torch.float8_e4m3fn)
+        vc = torch.zeros_like(kc)
+        slots = torch.randperm(blocks * 16, device="cuda")[:t].to(torch.int32)
+        one = torch.ones(1, device="cuda")
+        fn = lambda: ext.qk_norm_rope_cache_(q, k, v, qw, qw, pos, cache, kc, vc, slots, one, one)
     else:
         hq, hk = (int(v) for v in args.heads.split(","))
         q = torch.randn(t, hq, 128, device="cuda", generator=g).to(dt)
@@ -1036,7 +1062,7 @@ def main():
     parser.add_argument("--skip-cpu", action="store_true")
     parser.add_argument("--step-only", action="store_true",
                         help="run warm-up and the timed steps only (launch-list captures)")
-    parser.add_argument("--profile", choices=["fused", "rms", "qkkv", "qk"],
+    parser.add_argument("--profile", choices=["fused", "rms", "qkkv", "qk", "qkcache", "quant"],
                         help="launch one operator at one shape and exit (ncu driver)")
     parser.add_argument("--tokens", type=int, default=1024)
     parser.add_argument("--hidden", type=int, default=4096)
