@@ -697,6 +697,37 @@ def extension_suite(flush: Flusher, dist: Dist, args) -> dict:
     quant_case("fused_add_rms_norm_static_fp8_quant prefill bf16 65536x8192", 65536, 8192, True,
                False)
 
+    # RMSNorm + NVFP4 (e2m1 values, e4m3 scales per 16 elements, tiled scales)
+    def fp4_case(name, t, h):
+        nbytes = t * h * 2 * 3 + t * h // 2 + t * h // 16 + h * 2
+        w = (1 + 0.1 * torch.randn(h, device="cuda", generator=g)).to(bf)
+        gscale = torch.full((1,), 448.0 * 6.0 / 8.0, device="cuda")
+        sets = []
+        for _ in range(sets_for(nbytes)):
+            x = torch.randn(t, h, device="cuda", generator=g).to(bf)
+            r = torch.randn(t, h, device="cuda", generator=g).to(bf)
+            q = torch.empty(t, h // 2, device="cuda", dtype=torch.uint8)
+            sc = torch.empty(ext.nvfp4_scale_bytes(t, h), device="cuda", dtype=torch.uint8)
+            sets.append((x, r, q, sc))
+        record(name, [lambda s=s: ext.rms_norm_nvfp4_quant(s[2], s[3], s[0], w, gscale, EPS, s[1])
+                      for s in sets], nbytes)
+        if vllm is not None:
+            C, _ = vllm
+            scale_i32 = [torch.empty(sc.numel() // 4, device="cuda", dtype=torch.int32)
+                         for (_, _, _, sc) in sets]
+
+            def theirs(x, r, q, sc32):
+                C.fused_add_rms_norm(x, r, w, EPS)
+                C.scaled_fp4_quant.out(x, gscale, True, output=q, output_scale=sc32)
+
+            record(name + " [vLLM fused_add_rms_norm + scaled_fp4_quant]",
+                   [lambda s=s, sc32=sc32: theirs(s[0], s[1], s[2], sc32)
+                    for s, sc32 in zip(sets, scale_i32)], nbytes, comparator=True)
+        del sets
+
+    fp4_case("fused add + rms_norm_nvfp4_quant bf16 1024x4096", 1024, 4096)
+    fp4_case("fused add + rms_norm_nvfp4_quant prefill bf16 65536x8192", 65536, 8192)
+
     # the headline op beside vLLM's residual add + RMSNorm on the same shapes
     if vllm is not None:
         import sm120_rmsnorm as ops

@@ -23,11 +23,12 @@
  * Aliasing: output may equal input and residual_output may equal residual
  * (the in-place form). Any other overlap between buffers is undefined.
  *
- * The last two entry points (sm120n_qk_norm_rope_cache,
- * sm120n_rms_norm_fp8_quant) go beyond the reference's surface: they serve an
+ * The last three entry points (sm120n_qk_norm_rope_cache,
+ * sm120n_rms_norm_fp8_quant, sm120n_rms_norm_fp4_quant) go beyond the
+ * reference's surface: they serve an
  * inference engine around the same hot path (general head sizes and partial
  * rotary, Q/K/V as strided views of one QKV projection output, NHD / HND
- * paged caches, fp8 KV caches, RMSNorm feeding an fp8 GEMM). Their math is
+ * paged caches, fp8 KV caches, RMSNorm feeding an fp8 or NVFP4 GEMM). Their math is
  * the reference's, generalised; each states its exact definition.
  */
 #ifndef SM120NORM_B200_H_
@@ -39,7 +40,7 @@
 extern "C" {
 #endif
 
-#define SM120N_ABI_VERSION 2
+#define SM120N_ABI_VERSION 3
 
 #if defined(__GNUC__)
 #define SM120N_API __attribute__((visibility("default")))
@@ -264,6 +265,43 @@ SM120N_API int sm120n_rms_norm_fp8_quant(const void* input, const void* residual
                               float* token_scales, const float* scale_ub,
                               int64_t rows, int64_t hidden_size, int dtype,
                               float epsilon, void* stream);
+
+/* Layout of NVFP4 block scales (one e4m3 byte per 16 elements of a row).
+ * ROW_MAJOR: [rows, hidden / 16]. TILED_128X4: the layout block-scaled
+ * tensor-core GEMMs read -- rows padded to a multiple of 128 and blocks to a
+ * multiple of 4; the (row / 128, block / 4) tiles follow each other row of
+ * tiles by row of tiles, and inside a 512-byte tile row m, block k sits at
+ * ((m % 32) * 4 + (m % 128) / 32) * 4 + k % 4. The buffer then holds
+ * round_up(rows, 128) * round_up(hidden / 16, 4) bytes; padding entries are
+ * not written. */
+typedef enum sm120n_scale_layout {
+  SM120N_SCALES_ROW_MAJOR = 0,
+  SM120N_SCALES_TILED_128X4 = 1
+} sm120n_scale_layout;
+
+/*
+ * RMSNorm (optionally after a residual add) with an NVFP4 output for a
+ * block-scaled fp4 GEMM. y is computed as in sm120n_rms_norm_fp8_quant; then
+ * for every block of 16 consecutive elements of a row, with g = global_scale[0]
+ * and each step one IEEE fp32 operation:
+ *   a = max |y|;  s = e4m3(g * (a * c));  r = (s == 0) ? 0 : g / s;
+ *   (c = 1/6 rounded to fp32)
+ *   q = e2m1(y * r)   (e2m1 magnitudes 0, 0.5, 1, 1.5, 2, 3, 4, 6; both
+ *                      conversions round to nearest even and saturate)
+ * output: [rows, hidden / 2] bytes, element 2i in the low nibble;
+ * block_scales: e4m3 bytes in `scale_layout` (sm120n_scale_layout).
+ * hidden_size must be a multiple of 16; input, residual and weight 16-byte
+ * aligned, output 4-byte aligned (2-byte for fp32). residual_output may equal
+ * residual. No reference counterpart: the NVFP4 activation quantisation that
+ * follows rms_norm_out_cuda (csrc/rmsnorm_kernels.cu:482-524) and
+ * fused_add_rms_norm_out_cuda (:724-801) in an fp4 inference engine.
+ */
+SM120N_API int sm120n_rms_norm_fp4_quant(const void* input, const void* residual,
+                              const void* weight, void* residual_output,
+                              void* output, void* block_scales,
+                              const float* global_scale, int64_t rows,
+                              int64_t hidden_size, int dtype, float epsilon,
+                              int scale_layout, void* stream);
 
 #ifdef __cplusplus
 }

@@ -179,3 +179,69 @@ def rms_norm_fp8_quant(x, weight, eps=1e-6, residual=None, scale=None, scale_ub=
     y, residual_out = rms_norm_rows(x, weight, eps, residual)
     q, token_scales = quantise_rows(y, scale, scale_ub)
     return q, token_scales, residual_out
+
+
+# ---- NVFP4 (e2m1 values, e4m3 block scales) -----------------------------------------
+E2M1_MAGNITUDES = np.array([0.0, 0.5, 1.0, 1.5, 2.0, 3.0, 4.0, 6.0], dtype=np.float64)
+
+
+def e2m1_codes(values: np.ndarray) -> np.ndarray:
+    """4-bit e2m1 codes of fp32 values from the format definition (1 sign bit,
+    2 exponent bits, 1 mantissa bit; magnitudes 0, 0.5, 1, 1.5, 2, 3, 4, 6):
+    nearest magnitude, ties to the even code, saturating at 6, sign kept (so
+    small negatives give -0, code 8)."""
+    v = values.astype(np.float64)
+    mag = np.minimum(np.abs(v), 6.0)
+    dist = np.abs(mag[..., None] - E2M1_MAGNITUDES)
+    best = dist.min(axis=-1, keepdims=True)
+    ties = dist == best
+    # among tied magnitudes prefer the even code
+    even = ties & (np.arange(8) % 2 == 0)
+    choice = np.where(even.any(axis=-1, keepdims=True), even, ties)
+    code = np.argmax(choice, axis=-1).astype(np.uint8)
+    return np.where(np.signbit(v), code | 8, code).astype(np.uint8)
+
+
+def nvfp4_scale_offsets(rows: int, blocks: int, tiled: bool) -> np.ndarray:
+    """Byte offset of scale (row m, block k) in the row-major or the 128 x 4
+    tiled layout ([rows, blocks] array of offsets)."""
+    m = np.arange(rows)[:, None]
+    k = np.arange(blocks)[None, :]
+    if not tiled:
+        return m * blocks + k
+    columns = (blocks + 3) // 4 * 4
+    tile = (m // 128) * (columns // 4) + k // 4
+    return tile * 512 + ((m % 32) * 4 + (m % 128) // 32) * 4 + k % 4
+
+
+def nvfp4_quantise(y: torch.Tensor, global_scale: float, tiled: bool):
+    """(packed [rows, hidden / 2] uint8, scale bytes) of a normalised row
+    tensor y; the scale buffer is sized for the layout, padding zero."""
+    yf = y.float().reshape(-1, y.shape[-1]).numpy()
+    rows, hidden = yf.shape
+    blocks = hidden // 16
+    g = np.float32(global_scale)
+    peak = np.abs(yf.reshape(rows, blocks, 16)).max(axis=-1)
+    one_sixth = np.float32(1.0) / np.float32(6.0)
+    wanted = (g * (peak * one_sixth).astype(np.float32)).astype(np.float32)
+    codes = fp8_e4m3(torch.from_numpy(wanted)).view(torch.uint8).numpy()
+    s = torch.from_numpy(codes).view(torch.float8_e4m3fn).float().numpy()
+    with np.errstate(divide="ignore"):
+        r = np.where(s == 0, np.float32(0.0), g / np.where(s == 0, np.float32(1), s)).astype(np.float32)
+    v = (yf.reshape(rows, blocks, 16) * r[..., None]).astype(np.float32).reshape(rows, hidden)
+    q = e2m1_codes(v)
+    packed = (q[:, 0::2] | (q[:, 1::2] << 4)).astype(np.uint8)
+    if tiled:
+        size = (rows + 127) // 128 * 128 * ((blocks + 3) // 4 * 4)
+    else:
+        size = rows * blocks
+    scales = np.zeros(size, dtype=np.uint8)
+    scales[nvfp4_scale_offsets(rows, blocks, tiled)] = codes
+    return torch.from_numpy(packed), torch.from_numpy(scales)
+
+
+def rms_norm_nvfp4_quant(x, weight, global_scale, eps=1e-6, residual=None, tiled=True):
+    """(packed, scales, residual_out) of the NVFP4 norm operator."""
+    y, residual_out = rms_norm_rows(x, weight, eps, residual)
+    packed, scales = nvfp4_quantise(y, global_scale, tiled)
+    return packed, scales, residual_out

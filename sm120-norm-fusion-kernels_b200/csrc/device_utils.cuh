@@ -218,6 +218,21 @@ __device__ __forceinline__ float group_allreduce_sum(float v) {
   return v;
 }
 
+// Block-wide sum with one barrier; `partial` is double buffered by `parity`
+// so the next row's writes cannot race this row's reads.
+__device__ __forceinline__ float block_allreduce_sum(float v, float (*partial)[kWarpSize],
+                                                     int parity) {
+  const int lane = threadIdx.x & (kWarpSize - 1);
+  const int warp = threadIdx.x / kWarpSize;
+  const int warps = blockDim.x / kWarpSize;
+  v = group_allreduce_sum<kWarpSize>(v);
+  if (lane == 0) partial[parity][warp] = v;
+  __syncthreads();
+  float total = 0.0f;
+  for (int i = 0; i < warps; ++i) total = __fadd_rn(total, partial[parity][i]);
+  return total;
+}
+
 __device__ __forceinline__ float accumulate_squares(float acc, const float* f, int n) {
 #pragma unroll
   for (int i = 0; i < n; ++i) acc = __fadd_rn(acc, __fmul_rn(f[i], f[i]));

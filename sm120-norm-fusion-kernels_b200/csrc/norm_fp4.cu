@@ -1,0 +1,375 @@
+// norm_fp4.cu -- RMSNorm (optionally after the residual add) with an NVFP4
+// output, for B200 (sm_100a); C-ABI entry point sm120n_rms_norm_fp4_quant.
+//
+// The normalised row y is the one sm120n_rms_norm / sm120n_fused_add_rms_norm
+// produce (reference project, sm120_rmsnorm/reference.py:5-24); it is then
+// quantised for a block-scaled fp4 GEMM instead of being stored. Per block of
+// 16 consecutive elements of a row, with the caller's fp32 global scale g and
+// every step one IEEE fp32 operation:
+//   a = max |y|                         (exact)
+//   s = e4m3(g * (a * c))               (c = 1/6 rounded to fp32; saturating,
+//                                        nearest even)
+//   r = s == 0 ? 0 : g / s              (IEEE division)
+//   q = e2m1(y * r)                     (saturating at 6, nearest even)
+// q is packed two per byte, element 2i in the low nibble; s is stored as one
+// e4m3 byte per block, either row-major [rows, hidden / 16] or in the 128 x 4
+// tiled layout that block-scaled tensor-core GEMMs read: rows padded to 128
+// and blocks to 4, tile (rows / 128, blocks / 4) stored as [32][4][4] with
+// byte offset ((m % 32) * 4 + (m % 128) / 32) * 4 + k % 4 inside the tile.
+//
+// Kernels: a block per row with the row held in registers (rows up to 2048
+// 16-byte packs) and a vectorised two-pass kernel for wider rows. A 16-element
+// block spans 2 packs of a 16-bit type (4 of fp32) held by adjacent lanes, so
+// its maximum takes one (two) shuffles and no extra barrier. r takes one of
+// 256 values (one per e4m3 code): blocks that process many rows divide once
+// per code into a shared-memory table, so their per-block work has no
+// division; blocks with a row or two divide per block instead (filling the
+// table would cost more than it saves).
+#include <cuda_fp4.h>
+#include <cuda_fp8.h>
+
+#include <algorithm>
+
+#include "device_utils.cuh"
+#include "runtime.h"
+
+namespace sm120n {
+namespace {
+
+constexpr int kBlockElems = 16;
+constexpr float kOneSixth = 1.0f / 6.0f;  // rounded to fp32 at compile time
+
+template <typename T>
+struct Fp4Args {
+  const T* input;
+  const T* residual;  // nullptr: plain RMSNorm
+  const T* weight;
+  T* residual_output;
+  uint8_t* output;        // [rows, hidden / 2]
+  uint8_t* block_scales;  // e4m3, layout per `tiled`
+  const float* global_scale;
+  int64_t rows;
+  int hidden;
+  int scale_columns;  // hidden / 16, padded to 4 when tiled
+  bool tiled;
+  float epsilon;
+};
+
+__device__ __forceinline__ int64_t scale_offset(int64_t row, int block, int columns, bool tiled) {
+  if (!tiled) return row * columns + block;
+  const int64_t tile = (row / 128) * (columns / 4) + block / 4;
+  return tile * 512 + ((row % 32) * 4 + (row % 128) / 32) * 4 + block % 4;
+}
+
+// r = g / s for the e4m3 code of s.
+__device__ __forceinline__ float multiplier_of(uint8_t code, float g) {
+  const __half_raw h = __nv_cvt_fp8_to_halfraw(static_cast<__nv_fp8_storage_t>(code), __NV_E4M3);
+  const float s = __half2float(__half(h));
+  return s == 0.0f ? 0.0f : __fdiv_rn(g, s);
+}
+
+// r = g / s for every e4m3 code s (0 for s = 0), one entry per thread,
+// visible to the block after the caller's barrier.
+__device__ __forceinline__ void fill_multipliers(float* table, float g) {
+  for (int code = threadIdx.x; code < 256; code += blockDim.x) {
+    table[code] = multiplier_of(static_cast<uint8_t>(code), g);
+  }
+}
+
+// Block scale s (as an e4m3 byte) of a block whose largest magnitude is `peak`.
+__device__ __forceinline__ uint8_t block_scale(float peak, float g) {
+  return static_cast<uint8_t>(
+      __nv_cvt_float_to_fp8(__fmul_rn(g, __fmul_rn(peak, kOneSixth)), __NV_SATFINITE, __NV_E4M3));
+}
+
+// e2m1 codes of one pack of y times r, two per byte (element 2i low), as the
+// low Pack<T>::kElems / 2 bytes of the result.
+template <typename T>
+__device__ __forceinline__ uint32_t fp4_pack(const uint4& y, float r) {
+  float f[Pack<T>::kElems];
+  Pack<T>::to_f32(y, f);
+  uint32_t out = 0;
+#pragma unroll
+  for (int i = 0; i < Pack<T>::kElems / 2; ++i) {
+    const float2 v = make_float2(__fmul_rn(f[2 * i], r), __fmul_rn(f[2 * i + 1], r));
+    const uint32_t b = __nv_cvt_float2_to_fp4x2(v, __NV_E2M1, cudaRoundNearest);
+    out |= (b & 0xffu) << (8 * i);
+  }
+  return out;
+}
+
+template <typename T>
+__device__ __forceinline__ float pack_peak(const uint4& y) {
+  float f[Pack<T>::kElems];
+  Pack<T>::to_f32(y, f);
+  float m = 0.0f;
+#pragma unroll
+  for (int i = 0; i < Pack<T>::kElems; ++i) m = fmaxf(m, fabsf(f[i]));
+  return m;
+}
+
+// The largest magnitude of a 16-element block: packs of one block sit in
+// kLanes adjacent lanes (pack index and lane agree modulo kLanes).
+template <typename T>
+__device__ __forceinline__ float block_peak(float m) {
+  constexpr int kLanes = kBlockElems / Pack<T>::kElems;
+#pragma unroll
+  for (int offset = 1; offset < kLanes; offset <<= 1) {
+    m = fmaxf(m, __shfl_xor_sync(kFullMask, m, offset));
+  }
+  return m;
+}
+
+template <typename T>
+__device__ __forceinline__ void store_fp4(uint8_t* p, uint32_t v) {
+  if constexpr (Pack<T>::kElems == 8) {
+    *reinterpret_cast<uint32_t*>(p) = v;
+  } else {
+    *reinterpret_cast<uint16_t*>(p) = static_cast<uint16_t>(v);
+  }
+}
+
+// Quantise one pack c of row `row` (y already normalised); every lane of the
+// warp calls this (the shuffles need them all), `valid` marks real packs.
+// `multipliers`: the per-code table, or nullptr to divide here.
+template <typename T>
+__device__ __forceinline__ void quantise_fp4_pack(const Fp4Args<T>& a, int64_t row, int c,
+                                                  bool valid, const uint4& y, float g,
+                                                  const float* multipliers) {
+  constexpr int E = Pack<T>::kElems;
+  constexpr int kLanes = kBlockElems / E;
+  const float peak = block_peak<T>(valid ? pack_peak<T>(y) : 0.0f);
+  if (!valid) return;
+  const uint8_t code = block_scale(peak, g);
+  const float r = multipliers != nullptr ? multipliers[code] : multiplier_of(code, g);
+  store_fp4<T>(a.output + row * (a.hidden / 2) + static_cast<int64_t>(c) * (E / 2),
+               fp4_pack<T>(y, r));
+  if (c % kLanes == 0) {
+    a.block_scales[scale_offset(row, c / kLanes, a.scale_columns, a.tiled)] = code;
+  }
+}
+
+// kMinBlocks: resident blocks per SM the register budget must allow (left to
+// itself the compiler gives the four-pack, 256-thread shape 114 registers, 2
+// blocks per SM, and the two-pack, 512-thread shape 80, 1 block per SM; both
+// measured slower than the capped budgets).
+template <typename T, bool kAdd, int kPacksPerThread, int kMaxThreads, int kMinBlocks,
+          bool kTable>
+__global__ void __launch_bounds__(kMaxThreads, kMinBlocks) norm_fp4_cta_kernel(Fp4Args<T> a) {
+  constexpr int E = Pack<T>::kElems;
+  __shared__ float partial[2][kWarpSize];
+  __shared__ float multipliers[256];
+  wait_for_upstream_grid();
+  release_downstream_grid();
+  const int packs = a.hidden / E;
+  const float n = static_cast<float>(a.hidden);
+  const float g = *a.global_scale;
+  if constexpr (kTable) fill_multipliers(multipliers, g);  // read after the first barrier
+  uint4 w[kPacksPerThread];
+#pragma unroll
+  for (int i = 0; i < kPacksPerThread; ++i) {
+    const int c = threadIdx.x + i * blockDim.x;
+    if (c < packs) w[i] = load16(a.weight + static_cast<int64_t>(c) * E);
+  }
+  int parity = 0;
+  for (int64_t row = blockIdx.x; row < a.rows; row += gridDim.x) {
+    const int64_t base = row * a.hidden;
+    uint4 s[kPacksPerThread], r[kPacksPerThread];
+#pragma unroll
+    for (int i = 0; i < kPacksPerThread; ++i) {
+      const int c = threadIdx.x + i * blockDim.x;
+      if (c < packs) {
+        s[i] = load16(a.input + base + static_cast<int64_t>(c) * E);
+        if constexpr (kAdd) r[i] = load16(a.residual + base + static_cast<int64_t>(c) * E);
+      }
+    }
+    float2 acc = make_float2(0.0f, 0.0f);
+#pragma unroll
+    for (int i = 0; i < kPacksPerThread; ++i) {
+      const int c = threadIdx.x + i * blockDim.x;
+      if (c < packs) s[i] = combine_pack<T, kAdd>(s[i], r[i], acc);
+    }
+    const float inv = inverse_rms(block_allreduce_sum(__fadd_rn(acc.x, acc.y), partial, parity),
+                                  n, a.epsilon);
+    parity ^= 1;
+#pragma unroll
+    for (int i = 0; i < kPacksPerThread; ++i) {
+      const int c = threadIdx.x + i * blockDim.x;
+      const bool valid = c < packs;
+      uint4 y = make_uint4(0, 0, 0, 0);
+      if (valid) {
+        if constexpr (kAdd) store16(a.residual_output + base + static_cast<int64_t>(c) * E, s[i]);
+        y = normalise_pack<T>(s[i], w[i], inv);
+      }
+      quantise_fp4_pack<T>(a, row, c, valid, y, g, kTable ? multipliers : nullptr);
+    }
+  }
+}
+
+// Rows wider than the register kernel holds: pass 1 adds, stores the residual
+// and sums squares; pass 2 re-reads the packs this thread handled (now in L2)
+// and quantises them.
+template <typename T, bool kAdd>
+__global__ void __launch_bounds__(1024) norm_fp4_wide_kernel(Fp4Args<T> a) {
+  constexpr int E = Pack<T>::kElems;
+  __shared__ float partial[2][kWarpSize];
+  __shared__ float multipliers[256];
+  wait_for_upstream_grid();
+  release_downstream_grid();
+  const int packs = a.hidden / E;
+  const float n = static_cast<float>(a.hidden);
+  const float g = *a.global_scale;
+  fill_multipliers(multipliers, g);  // first read after the row's reduction barrier
+  const T* source = kAdd ? a.residual_output : a.input;
+  // every lane runs the same number of pass-2 iterations (the shuffles need
+  // the whole warp); blockDim.x is a multiple of the warp size
+  const int rounds = (packs + blockDim.x - 1) / blockDim.x;
+  int parity = 0;
+  for (int64_t row = blockIdx.x; row < a.rows; row += gridDim.x) {
+    const int64_t base = row * a.hidden;
+    float2 acc = make_float2(0.0f, 0.0f);
+    for (int c = threadIdx.x; c < packs; c += blockDim.x) {
+      const int64_t off = base + static_cast<int64_t>(c) * E;
+      uint4 r;
+      if constexpr (kAdd) r = load16(a.residual + off);
+      const uint4 s = combine_pack<T, kAdd>(load16(a.input + off), r, acc);
+      if constexpr (kAdd) store16(a.residual_output + off, s);
+    }
+    const float inv = inverse_rms(block_allreduce_sum(__fadd_rn(acc.x, acc.y), partial, parity),
+                                  n, a.epsilon);
+    parity ^= 1;
+    for (int k = 0; k < rounds; ++k) {
+      const int c = threadIdx.x + k * blockDim.x;
+      const bool valid = c < packs;
+      uint4 y = make_uint4(0, 0, 0, 0);
+      if (valid) {
+        y = normalise_pack<T>(load16(source + base + static_cast<int64_t>(c) * E),
+                              load16(a.weight + static_cast<int64_t>(c) * E), inv);
+      }
+      quantise_fp4_pack<T>(a, row, c, valid, y, g, multipliers);
+    }
+  }
+}
+
+template <typename Kernel>
+int fp4_grid(Kernel kernel, int threads, int64_t rows, int* grid) {
+  DeviceInfo dev;
+  int rc = current_device_info(&dev);
+  if (rc != SM120N_OK) return rc;
+  int resident = 1;
+  rc = max_resident_ctas(reinterpret_cast<const void*>(kernel), threads, 0, &resident);
+  if (rc != SM120N_OK) return rc;
+  *grid = static_cast<int>(
+      std::max<int64_t>(1, std::min<int64_t>(rows, static_cast<int64_t>(dev.sm_count) * resident)));
+  return SM120N_OK;
+}
+
+template <typename T, bool kAdd, int kPPT, int kMaxThreads, int kMinBlocks = 1,
+          bool kTable = false>
+int launch_fp4_cta(const Fp4Args<T>& a, int packs, cudaStream_t stream) {
+  auto kernel = norm_fp4_cta_kernel<T, kAdd, kPPT, kMaxThreads, kMinBlocks, kTable>;
+  const int threads = (((packs + kPPT - 1) / kPPT) + kWarpSize - 1) / kWarpSize * kWarpSize;
+  int grid = 0;
+  int rc = fp4_grid(kernel, threads, a.rows, &grid);
+  if (rc != SM120N_OK) return rc;
+  return launch(kernel, dim3(grid), dim3(threads), 0, stream, a);
+}
+
+template <typename T, bool kAdd>
+int run_fp4(const Fp4Args<T>& a, cudaStream_t stream) {
+  constexpr int E = Pack<T>::kElems;
+  const int packs = a.hidden / E;
+  // The same launch shapes as the fp8 kernels of this family.
+  DeviceInfo dev;
+  int rc = current_device_info(&dev);
+  if (rc != SM120N_OK) return rc;
+  const bool many_rows = a.rows >= 8 * static_cast<int64_t>(dev.sm_count);
+  if (packs <= 256) return launch_fp4_cta<T, kAdd, 1, 256>(a, packs, stream);
+  if (many_rows && packs > 512 && packs <= 1024) {
+    return launch_fp4_cta<T, kAdd, 4, 256, 3, true>(a, packs, stream);
+  }
+  if (packs <= 1024) return launch_fp4_cta<T, kAdd, 2, 512, 2>(a, packs, stream);
+  if (packs <= 2048) return launch_fp4_cta<T, kAdd, 4, 512>(a, packs, stream);
+  auto kernel = norm_fp4_wide_kernel<T, kAdd>;
+  int grid = 0;
+  rc = fp4_grid(kernel, 1024, a.rows, &grid);
+  if (rc != SM120N_OK) return rc;
+  return launch(kernel, dim3(grid), dim3(1024), 0, stream, a);
+}
+
+template <typename T>
+int run_fp4_typed(const void* input, const void* residual, const void* weight,
+                  void* residual_output, void* output, void* block_scales,
+                  const float* global_scale, int64_t rows, int64_t hidden, float epsilon,
+                  bool tiled, cudaStream_t stream) {
+  const int blocks = static_cast<int>(hidden / kBlockElems);
+  Fp4Args<T> a{static_cast<const T*>(input), static_cast<const T*>(residual),
+               static_cast<const T*>(weight), static_cast<T*>(residual_output),
+               static_cast<uint8_t*>(output), static_cast<uint8_t*>(block_scales), global_scale,
+               rows, static_cast<int>(hidden), tiled ? (blocks + 3) / 4 * 4 : blocks, tiled,
+               epsilon};
+  return residual != nullptr ? run_fp4<T, true>(a, stream) : run_fp4<T, false>(a, stream);
+}
+
+}  // namespace
+}  // namespace sm120n
+
+using namespace sm120n;
+
+extern "C" int sm120n_rms_norm_fp4_quant(const void* input, const void* residual,
+                                         const void* weight, void* residual_output, void* output,
+                                         void* block_scales, const float* global_scale,
+                                         int64_t rows, int64_t hidden_size, int dtype,
+                                         float epsilon, int scale_layout, void* stream) {
+  clear_error();
+  if (dtype_size(dtype) == 0) {
+    return fail(SM120N_ERR_INVALID_ARGUMENT, "supported dtypes are float16, bfloat16, and float32");
+  }
+  if (rows < 0) {
+    return fail(SM120N_ERR_INVALID_ARGUMENT, "rows must be non-negative (got %lld)",
+                static_cast<long long>(rows));
+  }
+  if (hidden_size <= 0 || hidden_size > (int64_t{1} << 30)) {
+    return fail(SM120N_ERR_INVALID_ARGUMENT, "hidden_size must be in [1, 2^30] (got %lld)",
+                static_cast<long long>(hidden_size));
+  }
+  if (hidden_size % kBlockElems != 0) {
+    return fail(SM120N_ERR_UNSUPPORTED,
+                "NVFP4 needs hidden_size to be a multiple of 16 (got %lld)",
+                static_cast<long long>(hidden_size));
+  }
+  if (scale_layout != SM120N_SCALES_ROW_MAJOR && scale_layout != SM120N_SCALES_TILED_128X4) {
+    return fail(SM120N_ERR_INVALID_ARGUMENT, "unknown scale_layout %d", scale_layout);
+  }
+  if ((residual == nullptr) != (residual_output == nullptr)) {
+    return fail(SM120N_ERR_INVALID_ARGUMENT, "residual and residual_output go together");
+  }
+  if (rows == 0) return SM120N_OK;
+  if (!input || !weight || !output || !block_scales || !global_scale) {
+    return fail(SM120N_ERR_INVALID_ARGUMENT,
+                "input, weight, output, block_scales and global_scale must be non-null");
+  }
+  const uintptr_t out_align = dtype == SM120N_F32 ? 2 : 4;
+  if (!aligned16(input) || !aligned16(weight) || (residual && !aligned16(residual)) ||
+      (residual_output && !aligned16(residual_output)) ||
+      (reinterpret_cast<uintptr_t>(output) % out_align) != 0) {
+    return fail(SM120N_ERR_UNSUPPORTED,
+                "NVFP4 quantisation needs 16-byte-aligned input, residual and weight and a "
+                "%d-byte-aligned output", static_cast<int>(out_align));
+  }
+  const cudaStream_t s = static_cast<cudaStream_t>(stream);
+  const bool tiled = scale_layout == SM120N_SCALES_TILED_128X4;
+  switch (dtype) {
+    case SM120N_F32:
+      return run_fp4_typed<float>(input, residual, weight, residual_output, output, block_scales,
+                                  global_scale, rows, hidden_size, epsilon, tiled, s);
+    case SM120N_F16:
+      return run_fp4_typed<__half>(input, residual, weight, residual_output, output,
+                                   block_scales, global_scale, rows, hidden_size, epsilon, tiled,
+                                   s);
+    default:
+      return run_fp4_typed<__nv_bfloat16>(input, residual, weight, residual_output, output,
+                                          block_scales, global_scale, rows, hidden_size, epsilon,
+                                          tiled, s);
+  }
+}

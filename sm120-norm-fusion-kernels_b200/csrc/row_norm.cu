@@ -101,21 +101,6 @@ __global__ void __launch_bounds__(256) row_norm_warp_kernel(RowArgs<T> a) {
   }
 }
 
-// Block-wide sum with one barrier; `partial` is double buffered by `parity`
-// so the next row's writes cannot race this row's reads.
-__device__ __forceinline__ float block_allreduce_sum(float v, float (*partial)[kWarpSize],
-                                                     int parity) {
-  const int lane = threadIdx.x & (kWarpSize - 1);
-  const int warp = threadIdx.x / kWarpSize;
-  const int warps = blockDim.x / kWarpSize;
-  v = group_allreduce_sum<kWarpSize>(v);
-  if (lane == 0) partial[parity][warp] = v;
-  __syncthreads();
-  float total = 0.0f;
-  for (int i = 0; i < warps; ++i) total = __fadd_rn(total, partial[parity][i]);
-  return total;
-}
-
 // ---- cta family --------------------------------------------------------------
 template <typename T, bool kAdd, int kPacksPerThread, int kMaxThreads>
 __global__ void __launch_bounds__(kMaxThreads) row_norm_cta_kernel(RowArgs<T> a) {

@@ -454,6 +454,46 @@ void b200_rms_norm_dynamic_per_token_quant(torch::Tensor result, torch::Tensor i
   run_norm_quant(result, input, residual, weight, nullptr, scale.data_ptr<float>(), ub, epsilon);
 }
 
+// RMSNorm (+ residual add) with NVFP4 output: `result` holds two e2m1 codes
+// per byte ([..., hidden / 2] bytes), `block_scale` one e4m3 byte per 16
+// elements (row-major, or the 128 x 4 tiled layout when `swizzled_scales`; any
+// dtype, e.g. the int32 buffers engines allocate for it, as long as it is
+// contiguous and large enough).
+void b200_rms_norm_nvfp4_quant(torch::Tensor result, torch::Tensor block_scale,
+                               torch::Tensor input, torch::Tensor weight,
+                               torch::Tensor global_scale, double epsilon,
+                               c10::optional<torch::Tensor> residual, bool swizzled_scales) {
+  check_activation_and_weight(input, weight);
+  const int64_t hidden = input.size(-1);
+  const int64_t rows = hidden == 0 ? 0 : input.numel() / hidden;
+  TORCH_CHECK(hidden % 16 == 0, "NVFP4 needs hidden_size to be a multiple of 16");
+  TORCH_CHECK(result.is_cuda() && result.is_contiguous() &&
+                  (result.scalar_type() == torch::kByte ||
+                   result.scalar_type() == at::ScalarType::Float4_e2m1fn_x2) &&
+                  result.numel() == rows * hidden / 2,
+              "result must be a contiguous CUDA uint8 tensor of rows x hidden / 2 bytes");
+  const int64_t blocks = hidden / 16;
+  const int64_t scale_bytes = swizzled_scales ? (rows + 127) / 128 * 128 * ((blocks + 3) / 4 * 4)
+                                              : rows * blocks;
+  TORCH_CHECK(block_scale.is_cuda() && block_scale.is_contiguous() &&
+                  block_scale.numel() * block_scale.element_size() >= scale_bytes,
+              "block_scale must be a contiguous CUDA tensor of at least ", scale_bytes, " bytes");
+  check_scalar_scale(global_scale, input, "global_scale");
+  TORCH_CHECK(result.device() == input.device() && block_scale.device() == input.device(),
+              "all tensors must be on the same CUDA device");
+  const void* residual_ptr = nullptr;
+  if (residual.has_value()) {
+    check_like_input(*residual, input, "residual");
+    residual_ptr = residual->data_ptr();
+  }
+  c10::cuda::CUDAGuard guard(input.device());
+  raise_if_failed(sm120n_rms_norm_fp4_quant(
+      input.data_ptr(), residual_ptr, weight.data_ptr(), const_cast<void*>(residual_ptr),
+      result.data_ptr(), block_scale.data_ptr(), global_scale.data_ptr<float>(), rows, hidden,
+      dtype_code(input), static_cast<float>(epsilon),
+      swizzled_scales ? SM120N_SCALES_TILED_128X4 : SM120N_SCALES_ROW_MAJOR, current_stream()));
+}
+
 TORCH_LIBRARY(sm120_norm_ext, m) {
   m.def(
       "qk_norm_rope_cache_(Tensor(a!) query, Tensor(b!) key, Tensor? value, "
@@ -470,6 +510,10 @@ TORCH_LIBRARY(sm120_norm_ext, m) {
   m.def(
       "rms_norm_dynamic_per_token_quant(Tensor(a!) result, Tensor input, Tensor weight, "
       "Tensor(b!) scale, float epsilon, Tensor? scale_ub, Tensor(c!)? residual) -> ()");
+  m.def(
+      "rms_norm_nvfp4_quant(Tensor(a!) result, Tensor(b!) block_scale, Tensor input, "
+      "Tensor weight, Tensor global_scale, float epsilon=1e-6, Tensor(c!)? residual=None, "
+      "bool swizzled_scales=True) -> ()");
 }
 
 TORCH_LIBRARY_IMPL(sm120_norm_ext, CUDA, m) {
@@ -477,6 +521,7 @@ TORCH_LIBRARY_IMPL(sm120_norm_ext, CUDA, m) {
   m.impl("rms_norm_static_fp8_quant", &b200_rms_norm_static_fp8_quant);
   m.impl("fused_add_rms_norm_static_fp8_quant", &b200_fused_add_rms_norm_static_fp8_quant);
   m.impl("rms_norm_dynamic_per_token_quant", &b200_rms_norm_dynamic_per_token_quant);
+  m.impl("rms_norm_nvfp4_quant", &b200_rms_norm_nvfp4_quant);
 }
 
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {

@@ -19,6 +19,7 @@ F32, F16, BF16 = 0, 1, 2
 OK, ERR_INVALID_ARGUMENT, ERR_UNSUPPORTED, ERR_CUDA = 0, 1, 2, 3
 ROPE_NEOX, ROPE_INTERLEAVED = 0, 1
 CACHE_AUTO, CACHE_FP8_E4M3 = 0, 1
+SCALES_ROW_MAJOR, SCALES_TILED_128X4 = 0, 1
 
 
 class QkCacheArgs(ctypes.Structure):
@@ -83,6 +84,8 @@ SIGNATURES: dict[str, tuple[list, object]] = {
     "sm120n_qk_norm_rope_cache": ([ctypes.POINTER(QkCacheArgs), _vp], _i32),
     "sm120n_rms_norm_fp8_quant": (
         [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _i64, _i64, _i32, _f32, _vp], _i32),
+    "sm120n_rms_norm_fp4_quant": (
+        [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _i64, _i64, _i32, _f32, _i32, _vp], _i32),
 }
 
 
@@ -178,3 +181,13 @@ def rms_norm_fp8_quant(input_ptr, residual_ptr, weight_ptr, residual_output_ptr,
     _check(load().sm120n_rms_norm_fp8_quant(
         input_ptr, residual_ptr, weight_ptr, residual_output_ptr, output_ptr, scale_ptr,
         token_scales_ptr, scale_ub_ptr, rows, hidden_size, dtype, epsilon, stream))
+
+
+def rms_norm_fp4_quant(input_ptr, residual_ptr, weight_ptr, residual_output_ptr, output_ptr,
+                       block_scales_ptr, global_scale_ptr, rows, hidden_size, dtype,
+                       epsilon=1e-6, scale_layout=SCALES_TILED_128X4, stream=0) -> None:
+    """RMSNorm (+ residual add) with NVFP4 output and e4m3 block scales; pass
+    0 / None for an absent residual (sm120n_rms_norm_fp4_quant)."""
+    _check(load().sm120n_rms_norm_fp4_quant(
+        input_ptr, residual_ptr, weight_ptr, residual_output_ptr, output_ptr, block_scales_ptr,
+        global_scale_ptr, rows, hidden_size, dtype, epsilon, scale_layout, stream))

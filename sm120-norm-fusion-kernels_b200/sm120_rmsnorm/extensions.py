@@ -20,6 +20,10 @@ kernels' numerics (csrc/head_cache.cu, csrc/norm_quant.cu):
   ``q = sat(y * (1 / scale))``, sat() clamping to +-448 and rounding to nearest
   even. The operator names and argument order are the ones fp8 inference
   engines use for these fusions.
+* :func:`rms_norm_nvfp4_quant` -- the same RMSNorm quantised to NVFP4 (e2m1
+  values, one e4m3 scale per 16 elements, a caller-supplied global scale),
+  with the block scales row-major or in the tiled layout of block-scaled
+  tensor-core GEMMs.
 
 Registered as ``torch.ops.sm120_norm_ext.*``; no fallback when the extension
 is missing.
@@ -93,6 +97,33 @@ def rms_norm_dynamic_per_token_quant(result: torch.Tensor, input: torch.Tensor,
         result, input, weight, scale, epsilon, scale_ub, residual)
 
 
+def rms_norm_nvfp4_quant(result: torch.Tensor, block_scale: torch.Tensor, input: torch.Tensor,
+                         weight: torch.Tensor, global_scale: torch.Tensor, epsilon: float = 1e-6,
+                         residual: torch.Tensor | None = None,
+                         swizzled_scales: bool = True) -> None:
+    """RMSNorm (after the residual add when ``residual`` is given, which is
+    then updated in place) quantised to NVFP4 for a block-scaled fp4 GEMM.
+    Per 16 elements of a row, with g = ``global_scale``:
+    ``s = e4m3(g * (max|y| * fp32(1/6)))``, ``q = e2m1(y * (g / s))`` (nearest even,
+    saturating). ``result``: ``[rows, hidden / 2]`` uint8, element 2i in the
+    low nibble; ``block_scale``: the e4m3 scales, row-major
+    ``[rows, hidden / 16]`` or, when ``swizzled_scales``, the 128 x 4 tiled
+    layout tensor-core GEMMs read (``round_up(rows, 128) *
+    round_up(hidden / 16, 4)`` bytes, padding untouched)."""
+    _extension()
+    torch.ops.sm120_norm_ext.rms_norm_nvfp4_quant(result, block_scale, input, weight,
+                                                  global_scale, epsilon, residual,
+                                                  swizzled_scales)
+
+
+def nvfp4_scale_bytes(rows: int, hidden: int, swizzled_scales: bool = True) -> int:
+    """Bytes of the block-scale buffer for ``rows`` x ``hidden``."""
+    blocks = hidden // 16
+    if not swizzled_scales:
+        return rows * blocks
+    return (rows + 127) // 128 * 128 * ((blocks + 3) // 4 * 4)
+
+
 if _C is not None:
     # Meta implementations: every operator only mutates its arguments.
 
@@ -115,4 +146,9 @@ if _C is not None:
     @torch.library.register_fake("sm120_norm_ext::rms_norm_dynamic_per_token_quant")
     def _rms_norm_dynamic_per_token_quant_meta(result, input, weight, scale, epsilon,
                                                scale_ub=None, residual=None) -> None:
+        return None
+
+    @torch.library.register_fake("sm120_norm_ext::rms_norm_nvfp4_quant")
+    def _rms_norm_nvfp4_quant_meta(result, block_scale, input, weight, global_scale,
+                                   epsilon=1e-6, residual=None, swizzled_scales=True) -> None:
         return None

@@ -243,3 +243,58 @@ def test_norm_quant_rejects_bad_arguments():
     with pytest.raises(capi.CApiError, match="hidden_size"):
         capi.rms_norm_fp8_quant(16, None, 16, None, 16, 16, None, None, 1, 0, capi.BF16)
     capi.rms_norm_fp8_quant(0, None, 0, None, 0, 16, None, None, 0, 64, capi.BF16)  # no rows
+
+
+# ---- NVFP4 ------------------------------------------------------------------------
+def test_e2m1_rounding_follows_the_format_definition():
+    values = np.array([0, 0.24, 0.25, 0.26, 0.75, 1.25, 1.75, 2.5, 3.5, 5, 5.1, 7, 100,
+                       -0.1, -0.0, -5, -0.75], dtype=np.float32)
+    # ties go to the even code: 0.25 -> 0, 0.75 -> 1.0, 1.25 -> 1.0, 1.75 -> 2,
+    # 2.5 -> 2, 3.5 -> 4, 5 -> 4; beyond 6 saturates; the sign bit is kept
+    want = [0, 0, 0, 1, 2, 2, 4, 4, 6, 6, 7, 7, 7, 8, 8, 14, 10]
+    assert ex.e2m1_codes(values).tolist() == want
+    decoded = ex.E2M1_MAGNITUDES[np.array(want) & 7]
+    assert decoded.max() == 6.0
+
+
+def test_tiled_scale_layout_is_the_128x4_block_interleave():
+    rows, blocks = 300, 10
+    offsets = ex.nvfp4_scale_offsets(rows, blocks, tiled=True)
+    # restated as a reshape: pad to (384, 12), view (tiles_m, 4, 32, tiles_k, 4),
+    # order the axes (tiles_m, tiles_k, 32, 4, 4)
+    padded = torch.full((384, 12), -1, dtype=torch.int64)
+    padded[:rows, :blocks] = torch.arange(rows * blocks).reshape(rows, blocks)
+    order = padded.reshape(3, 4, 32, 3, 4).permute(0, 3, 2, 1, 4).reshape(-1)
+    position = torch.empty(rows * blocks, dtype=torch.int64)
+    real = order >= 0
+    position[order[real]] = torch.nonzero(real).flatten()
+    assert np.array_equal(offsets.reshape(-1), position.numpy())
+    assert np.array_equal(ex.nvfp4_scale_offsets(rows, blocks, tiled=False).reshape(-1),
+                          np.arange(rows * blocks))
+
+
+def test_nvfp4_block_scales_and_values():
+    y = torch.zeros(1, 32, dtype=torch.bfloat16)
+    y[0, :16] = torch.tensor([3.0, -1.5, 0.0] + [0.25] * 13)
+    y[0, 16:] = 0.0  # an all-zero block: scale 0, values 0
+    packed, scales = ex.nvfp4_quantise(y, 2.0, tiled=False)
+    # block 0: peak 3, s = e4m3(2 * (3 * fp32(1/6))) = 1.0, r = g / s = 2: y * 2
+    assert scales.tolist() == [0x38, 0x00]  # 1.0 in e4m3 is 0x38
+    codes = np.stack([packed.numpy() & 0xF, packed.numpy() >> 4], -1).reshape(-1)
+    assert codes[:4].tolist() == [7, 13, 0, 1]  # 6, -3 (sign | code 5), 0, 0.5
+    assert codes[16:].tolist() == [0] * 16
+
+
+def test_fp4_quant_rejects_bad_arguments():
+    with pytest.raises(capi.CApiError, match="multiple of 16"):
+        capi.rms_norm_fp4_quant(16, None, 16, None, 16, 16, 16, 1, 72, capi.BF16)
+    with pytest.raises(capi.CApiError, match="unknown scale_layout"):
+        capi.rms_norm_fp4_quant(16, None, 16, None, 16, 16, 16, 1, 64, capi.BF16,
+                                scale_layout=5)
+    with pytest.raises(capi.CApiError, match="residual and residual_output go together"):
+        capi.rms_norm_fp4_quant(16, 16, 16, None, 16, 16, 16, 1, 64, capi.BF16)
+    with pytest.raises(capi.CApiError, match="16-byte-aligned"):
+        capi.rms_norm_fp4_quant(8, None, 16, None, 16, 16, 16, 1, 64, capi.BF16)
+    with pytest.raises(capi.CApiError, match="must be non-null"):
+        capi.rms_norm_fp4_quant(16, None, 16, None, 16, None, 16, 1, 64, capi.BF16)
+    capi.rms_norm_fp4_quant(0, None, 0, None, 0, 0, 0, 0, 64, capi.BF16)  # no rows

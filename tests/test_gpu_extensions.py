@@ -378,3 +378,90 @@ def test_norm_quant_empty_and_unaligned_output():
     extensions.rms_norm_static_fp8_quant(out, x.to(DEV), w.to(DEV), torch.tensor([0.05], device=DEV))
     want_q, _, _ = ex.rms_norm_fp8_quant(x, w, scale=torch.tensor([0.05]))
     assert torch.equal(out.cpu().view(torch.uint8), want_q.view(torch.uint8))
+
+
+# ---- RMSNorm + NVFP4 -----------------------------------------------------------------
+def run_fp4(x, w, g, residual=None, tiled=True):
+    rows, hidden = x.numel() // x.shape[-1], x.shape[-1]
+    out = torch.zeros(rows, hidden // 2, dtype=torch.uint8, device=DEV)
+    scales = torch.zeros(extensions.nvfp4_scale_bytes(rows, hidden, tiled), dtype=torch.uint8,
+                         device=DEV)
+    r_d = residual.to(DEV) if residual is not None else None
+    x_d = x.to(DEV)
+    extensions.rms_norm_nvfp4_quant(out, scales, x_d, w.to(DEV), torch.tensor([g], device=DEV),
+                                    1e-6, r_d, tiled)
+    assert torch.equal(x_d.cpu(), x), "input must not change"
+    return out.cpu(), scales.cpu(), (r_d.cpu() if r_d is not None else None)
+
+
+def e2m1_step_distance(a, b):
+    def nibbles(t):
+        t = t.to(torch.int16)
+        codes = torch.stack((t & 0xF, t >> 4), -1)
+        return torch.where(codes >= 8, -(codes & 7), codes)
+    return (nibbles(a) - nibbles(b)).abs()
+
+
+@pytest.mark.parametrize("dtype", DTYPES)
+@pytest.mark.parametrize("hidden", [64, 1024, 4096, 8192, 16384, 32768])
+@pytest.mark.parametrize("add", [False, True])
+@pytest.mark.parametrize("tiled", [True, False])
+def test_nvfp4_exact(dtype, hidden, add, tiled):
+    g = gen(hidden + add)
+    limit = 8 if add else 16
+    x = exact_values((37, hidden), dtype, g, limit)
+    r = exact_values((37, hidden), dtype, g, limit) if add else None
+    w = weights(hidden, dtype, g)
+    q, scales, r_out = run_fp4(x, w, 300.0, r, tiled)
+    want_q, want_scales, want_r = ex.rms_norm_nvfp4_quant(x, w, 300.0, residual=r, tiled=tiled)
+    assert torch.equal(scales, want_scales), "block scales"
+    assert torch.equal(q, want_q), "e2m1 codes"
+    if add:
+        assert_bitwise_equal(r_out, want_r, what="residual")
+
+
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
+def test_nvfp4_many_wide_rows_exact(dtype):
+    """1200 rows of 8192 (the persistent four-packs-per-thread launch), tiled
+    scales over a row count that is not a multiple of 128."""
+    g = gen(1200)
+    x = exact_values((1200, 8192), dtype, g, 8)
+    r = exact_values((1200, 8192), dtype, g, 8)
+    w = weights(8192, dtype, g)
+    q, scales, r_out = run_fp4(x, w, 500.0, r, True)
+    want_q, want_scales, want_r = ex.rms_norm_nvfp4_quant(x, w, 500.0, residual=r, tiled=True)
+    assert torch.equal(scales, want_scales)
+    assert torch.equal(q, want_q)
+    assert_bitwise_equal(r_out, want_r, what="residual")
+
+
+@pytest.mark.parametrize("dtype", DTYPES)
+@pytest.mark.parametrize("hidden", [1024, 8192, 32768])
+def test_nvfp4_random_inputs(dtype, hidden):
+    g = gen(11 + hidden)
+    x = torch.randn(64, hidden, generator=g).to(dtype)
+    r = torch.randn(64, hidden, generator=g).to(dtype)
+    w = weights(hidden, dtype, g)
+    q, scales, r_out = run_fp4(x, w, 400.0, r, False)
+    want_q, want_scales, want_r = ex.rms_norm_nvfp4_quant(x, w, 400.0, residual=r, tiled=False)
+    assert_bitwise_equal(r_out, want_r, what="residual")
+    scale_steps = e4m3_step_distance(scales, want_scales)
+    assert int(scale_steps.max()) <= 1
+    assert float((scale_steps > 0).float().mean()) < 0.01
+    same_scale = (scale_steps == 0).reshape(64, hidden // 16)
+    steps = e2m1_step_distance(q, want_q).reshape(64, hidden // 16, 16)
+    assert int(steps[same_scale].max()) <= 1
+
+
+def test_nvfp4_tensor_checks():
+    x = torch.randn(4, 72, device=DEV).to(torch.bfloat16)
+    w = torch.ones(72, device=DEV, dtype=torch.bfloat16)
+    out = torch.zeros(4, 36, dtype=torch.uint8, device=DEV)
+    scales = torch.zeros(4096, dtype=torch.uint8, device=DEV)
+    with pytest.raises(RuntimeError, match="multiple of 16"):
+        extensions.rms_norm_nvfp4_quant(out, scales, x, w, torch.ones(1, device=DEV))
+    x = torch.randn(4, 64, device=DEV).to(torch.bfloat16)
+    w = torch.ones(64, device=DEV, dtype=torch.bfloat16)
+    out = torch.zeros(4, 32, dtype=torch.uint8, device=DEV)
+    with pytest.raises(RuntimeError, match="block_scale must be"):
+        extensions.rms_norm_nvfp4_quant(out, scales[:100], x, w, torch.ones(1, device=DEV))
