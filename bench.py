@@ -421,6 +421,7 @@ def _measure_rest(args, dist, ops, flush, data, step_ms, launches_per_step) -> d
     per_op = {} if args.skip_per_op else per_op_suite(ops, flush, dist, args)
     extensions = {} if args.skip_per_op else extension_suite(flush, dist, args)
     engine = {} if args.skip_per_op else engine_suite(flush, dist, args)
+    projection = {} if args.skip_per_op else projection_suite(flush, dist, args)
 
     return {
         "metric": "achieved HBM GB/s (% of B200 peak) and us/call per op at 1/2/4/8 GPUs",
@@ -438,6 +439,7 @@ def _measure_rest(args, dist, ops, flush, data, step_ms, launches_per_step) -> d
                          "per-launch timing, outside the events"},
         "roofline": roofline, "e2e": e2e, "gpu_launches": launches_per_step * args.steps,
         "per_shape": per_shape, "per_op": per_op, "extensions": extensions, "engine": engine,
+        "projection": projection,
         "device": torch.cuda.get_device_name(dev),
     }
 
@@ -834,6 +836,13 @@ def engine_suite(flush: Flusher, dist: Dist, args) -> dict:
         ours.slot_mapping.copy_(slots)
         row["b200"] = time_graph_us(ours.graph)
         del ours
+        fused = DecodeGraph(layers, batch, cos_sin, kcs, vcs, fused_projection=True)
+        fused.hidden.copy_(torch.randn(batch, shape.hidden, device="cuda", generator=g).to(bf))
+        fused.residual.copy_(torch.randn(batch, shape.hidden, device="cuda", generator=g).to(bf))
+        fused.positions.copy_(positions)
+        fused.slot_mapping.copy_(slots)
+        row["b200_fused_projection"] = time_graph_us(fused.graph)
+        del fused
         base = generic_graph(batch, positions, slots, kcs, vcs, gemm_only)
         row["gemm_only"] = time_graph_us(base)
         del base
@@ -858,6 +867,61 @@ def engine_suite(flush: Flusher, dist: Dist, args) -> dict:
             entry["vllm_unavailable"] = row["vllm_unavailable"]
         out[f"decode B={batch}"] = entry
         del kcs, vcs
+    return out
+
+
+def projection_suite(flush: Flusher, dist: Dist, args) -> dict:
+    """The QKV projection of a Qwen3-8B-shaped layer (hidden 4096, 32/8 heads
+    of 128, bf16) at decode and prefill token counts: this package's
+    tensor-core GEMM alone and with the Q/K norm + RoPE + KV store fused into
+    its epilogue, against PyTorch's GEMM (cuBLAS) alone and followed by the
+    stand-alone Q/K kernel on the strided QKV views -- the unfused path the
+    fusion replaces. Same protocol as the other suites; TFLOP/s counts the
+    GEMM's 2 * T * N * K."""
+    from sm120_rmsnorm import extensions as ext
+
+    out = {}
+    reps = max(3, args.reps)
+    bf = torch.bfloat16
+    g = torch.Generator(device="cuda").manual_seed(41 + dist.rank)
+    hidden, hq, hk = 4096, 32, 8
+    n = (hq + 2 * hk) * 128
+    w = (torch.randn(n, hidden, device="cuda", generator=g) / hidden ** 0.5).to(bf)
+    qw = (1 + 0.1 * torch.randn(128, device="cuda", generator=g)).to(bf)
+    kw = (1 + 0.1 * torch.randn(128, device="cuda", generator=g)).to(bf)
+    inv = 1.0 / (1e6 ** (torch.arange(0, 128, 2, dtype=torch.float32, device="cuda") / 128))
+    f = torch.outer(torch.arange(32768, dtype=torch.float32, device="cuda"), inv)
+    table = torch.cat((f.cos(), f.sin()), dim=-1)
+    for t in (1, 64, 256, 4096, 32768):
+        x = torch.randn(t, hidden, device="cuda", generator=g).to(bf)
+        qkv = torch.empty(t, n, device="cuda", dtype=bf)
+        pos = torch.randint(0, 32768, (t,), device="cuda", generator=g)
+        slots_total = max(4 * t, 4096)
+        slots = torch.randperm(slots_total, device="cuda", generator=g)[:t].to(torch.int32)
+        kc = torch.zeros(slots_total, hk, 128, device="cuda", dtype=bf)
+        vc = torch.zeros_like(kc)
+        views = (qkv[:, :hq * 128].view(t, hq, 128), qkv[:, hq * 128:(hq + hk) * 128].view(t, hk, 128),
+                 qkv[:, (hq + hk) * 128:].view(t, hk, 128))
+        flops = 2.0 * t * n * hidden
+        cases = {
+            "cublas_gemm": lambda: torch.matmul(x, w.t(), out=qkv),
+            "own_gemm": lambda: ext.qkv_proj_norm_rope_cache_(x, w, qkv, hq, hk, fuse_norm=False),
+            "cublas_gemm_then_qk_kernel": lambda: (
+                torch.matmul(x, w.t(), out=qkv),
+                ext.qk_norm_rope_cache_(views[0], views[1], views[2], qw, kw, pos, table,
+                                        kc.view(-1, 1, hk, 128), vc.view(-1, 1, hk, 128),
+                                        slots)),
+            "fused_projection": lambda: ext.qkv_proj_norm_rope_cache_(
+                x, w, qkv, hq, hk, qw, kw, pos, table, kc, vc, slots),
+        }
+        entry = {}
+        for name, fn in cases.items():
+            graph, _ = capture([fn])
+            us = dist.max(time_graph(graph, flush, reps))
+            entry[name] = {"us": round(us, 2), "tflops": round(flops / (us * 1e-6) / 1e12, 1)}
+            del graph
+        out[f"tokens={t}"] = entry
+        del x, qkv, kc, vc
     return out
 
 

@@ -23,12 +23,14 @@
  * Aliasing: output may equal input and residual_output may equal residual
  * (the in-place form). Any other overlap between buffers is undefined.
  *
- * The last three entry points (sm120n_qk_norm_rope_cache,
- * sm120n_rms_norm_fp8_quant, sm120n_rms_norm_fp4_quant) go beyond the
- * reference's surface: they serve an
+ * The last four entry points (sm120n_qk_norm_rope_cache,
+ * sm120n_rms_norm_fp8_quant, sm120n_rms_norm_fp4_quant,
+ * sm120n_qkv_proj_norm_rope_cache) go beyond the reference's surface: they
+ * serve an
  * inference engine around the same hot path (general head sizes and partial
  * rotary, Q/K/V as strided views of one QKV projection output, NHD / HND
- * paged caches, fp8 KV caches, RMSNorm feeding an fp8 or NVFP4 GEMM). Their math is
+ * paged caches, fp8 KV caches, RMSNorm feeding an fp8 or NVFP4 GEMM, the QKV
+ * projection with the Q/K norm in its epilogue). Their math is
  * the reference's, generalised; each states its exact definition.
  */
 #ifndef SM120NORM_B200_H_
@@ -40,7 +42,7 @@
 extern "C" {
 #endif
 
-#define SM120N_ABI_VERSION 3
+#define SM120N_ABI_VERSION 4
 
 #if defined(__GNUC__)
 #define SM120N_API __attribute__((visibility("default")))
@@ -302,6 +304,32 @@ SM120N_API int sm120n_rms_norm_fp4_quant(const void* input, const void* residual
                               const float* global_scale, int64_t rows,
                               int64_t hidden_size, int dtype, float epsilon,
                               int scale_layout, void* stream);
+
+/*
+ * The QKV projection of an attention layer on the tensor cores, with the
+ * Q/K RMSNorm + RoPE + KV store of sm120n_fused_qk_rms_norm_rope_kv fused into
+ * its epilogue (bf16, head_dim 128, half-split RoPE over all 128 elements):
+ *   qkv[t, :] = round_bf16(hidden[t, :] @ qkv_weight^T)   (fp32 accumulation)
+ *   epilogue 1: then, on the [tokens, Hq + 2 * Hk, 128] view of qkv, exactly
+ *   what sm120n_fused_qk_rms_norm_rope_kv does (in place on the Q and K heads,
+ *   rotated K and V stored at slot_mapping[t] of the [cache_slots, Hk, 128]
+ *   caches; pass null caches / slot_mapping for no store); epilogue 0: the
+ *   plain GEMM.
+ * hidden [tokens, hidden_size], qkv_weight [(Hq + 2Hk) * 128, hidden_size] and
+ * qkv [tokens, (Hq + 2Hk) * 128] are dense row-major bf16, 16-byte aligned;
+ * hidden_size a multiple of 64; Hq + 2Hk even. The result of epilogue 1 is
+ * bit-identical to epilogue 0 followed by sm120n_fused_qk_rms_norm_rope_kv on
+ * qkv.
+ * Generalises the caller of csrc/rmsnorm_kernels.cu:611-709: the reference
+ * runs that operator after a separate projection GEMM.
+ */
+SM120N_API int sm120n_qkv_proj_norm_rope_cache(
+    const void* hidden, const void* qkv_weight, void* qkv, int64_t tokens,
+    int64_t hidden_size, int64_t query_heads, int64_t key_heads,
+    const void* query_weight, const void* key_weight, const int64_t* positions,
+    const float* cos_sin_cache, int64_t rope_positions, void* key_cache,
+    void* value_cache, const int32_t* slot_mapping, int64_t cache_slots,
+    float epsilon, int epilogue, void* stream);
 
 #ifdef __cplusplus
 }

@@ -30,7 +30,7 @@ BUILD = ROOT / "_build"
 CUDA_HOME = Path(os.environ.get("CUDA_HOME", "/usr/local/cuda"))
 NVCC = str(CUDA_HOME / "bin" / "nvcc")
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
-CUDA_SOURCES = ["runtime.cu", "row_norm.cu", "head_norm_rope.cu", "head_cache.cu", "norm_quant.cu", "norm_fp4.cu"]
+CUDA_SOURCES = ["runtime.cu", "row_norm.cu", "head_norm_rope.cu", "head_cache.cu", "norm_quant.cu", "norm_fp4.cu", "qkv_gemm.cu"]
 NVCC_FLAGS = [
     "-O3", "-std=c++17", "-lineinfo", "--expt-relaxed-constexpr",
     "-Xcompiler", "-fPIC", "-Xcompiler", "-fvisibility=hidden",

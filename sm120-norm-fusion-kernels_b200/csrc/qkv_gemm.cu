@@ -1,0 +1,518 @@
+// qkv_gemm.cu -- the QKV projection of an attention layer on the sm_100
+// tensor cores with the Q/K RMSNorm + RoPE + paged KV store fused into its
+// epilogue; C-ABI entry point sm120n_qkv_proj_norm_rope_cache.
+//
+//   qkv[t, :] = hidden[t, :] @ qkv_weight.T          (bf16 in, fp32 accumulate,
+//                                                      rounded to bf16)
+// then, per 128-wide head of qkv (Hq query, Hk key, Hk value heads), exactly
+// what fused_qk_rms_norm_rope_kv does to a bf16 [T, H, 128] tensor (reference
+// project, csrc/rmsnorm_kernels.cu:611-709; math of sm120_rmsnorm/
+// reference.py:27-49): RMSNorm rounded twice, half-split RoPE, rotated K and
+// V stored at slot_mapping[t] of a [slots, Hk, 128] cache.
+//
+// Tiling: one thread block per 128-token x kTileN-column tile (one or two
+// heads), four warps. The K dimension streams through kStages shared-memory
+// stages of 128-row (A) and kTileN-row (B) x 64-element boxes, loaded by the
+// TMA engine with 128-byte swizzling (thread 0 of warp 0) and consumed by
+// tcgen05.mma.kind::f16 (M 128, N kTileN, K 16; issued by thread 0 of warp 1)
+// into kTileN columns of tensor memory. tcgen05.commit releases each stage
+// back to the loader and finally signals the epilogue.
+//
+// Epilogue: warp w reads TMEM lanes 32w..32w+31, i.e. each thread owns one
+// token row of the tile and, per head, all 128 accumulators of that row. It
+// rounds them to bf16 (the GEMM output), sums squares in the order the
+// stand-alone Q/K kernel uses (eight 16-element lane slices, pairwise
+// butterfly), and then applies the same normalise / rotate helpers, so the
+// result is bit-identical to this kernel's plain GEMM followed by
+// fused_qk_rms_norm_rope_kv / qk_norm_rope_cache_ on its output.
+//
+// Every wait on an mbarrier is bounded; an expired wait increments a device
+// counter (read with sm120n_get_device_faults), the block skips the rest of
+// its work (waiting, again bounded, for its own asynchronous operations) and
+// releases its tensor memory.
+#include <cuda.h>
+#include <cudaTypedefs.h>
+
+#include <algorithm>
+#include <mutex>
+
+#include "head_utils.cuh"
+#include "runtime.h"
+
+namespace sm120n {
+
+__device__ unsigned int g_gemm_expired_waits = 0;
+
+namespace {
+
+constexpr int kTileM = 128;
+constexpr int kTileK = 64;    // 128 bytes of bf16: one swizzle row
+constexpr int kMmaK = 16;
+constexpr int kHead = 128;
+constexpr uint32_t kABytes = kTileM * kTileK * 2;  // 16 KiB
+
+// Launch shape: kTileN output columns (one or two heads) per block, kStages
+// pipeline stages, kWarps warps (4 or 8; with 8 the epilogue splits the heads
+// of a tile over two warp groups that read the same TMEM lanes).
+template <int kTileN, int kStages, int kWarps>
+struct Shape {
+  static constexpr int kThreads = kWarps * kWarpSize;
+  static constexpr uint32_t kBBytes = kTileN * kTileK * 2;
+  static constexpr uint32_t kStageBytes = kABytes + kBBytes;
+  static constexpr int kTmemColumns = kTileN;  // fp32 accumulator columns
+  static constexpr int kHeads = kTileN / kHead;
+  static constexpr size_t kSmem = static_cast<size_t>(kStages) * kStageBytes + 1024;
+  // Instruction descriptor of tcgen05.mma.kind::f16: fp32 accumulator
+  // (bit 4), bf16 A and B (bits 7 and 10), both K-major, N >> 3 at bit 17,
+  // M >> 4 at bit 24.
+  static constexpr uint32_t kInstrDesc = (1u << 4) | (1u << 7) | (1u << 10) |
+                                         (static_cast<uint32_t>(kTileN >> 3) << 17) |
+                                         (static_cast<uint32_t>(kTileM >> 4) << 24);
+};
+
+struct GemmArgs {
+  __nv_bfloat16* qkv;  // [tokens, N] output
+  const __nv_bfloat16* query_weight;
+  const __nv_bfloat16* key_weight;
+  const int64_t* positions;
+  const float* cos_sin;
+  __nv_bfloat16* key_cache;
+  __nv_bfloat16* value_cache;
+  const int32_t* slots;
+  int64_t tokens;
+  int64_t rope_positions;
+  int64_t cache_slots;
+  int k_tiles;
+  int query_heads;
+  int key_heads;
+  int n;  // (Hq + 2Hk) * 128
+  float epsilon;
+  int epilogue;  // 0: store the bf16 GEMM output only; 1: norm + RoPE + cache
+};
+
+// ---- PTX wrappers ----------------------------------------------------------
+__device__ __forceinline__ void tma_load_2d(void* smem_dst, const CUtensorMap* map, int x, int y,
+                                            uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes"
+      " [%0], [%1, {%2, %3}], [%4];" ::"r"(shared_address(smem_dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(shared_address(bar))
+      : "memory");
+}
+
+__device__ __forceinline__ void tmem_alloc(uint32_t* slot, uint32_t columns) {
+  asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
+                   shared_address(slot)),
+               "r"(columns)
+               : "memory");
+  asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+}
+
+__device__ __forceinline__ void tmem_dealloc(uint32_t taddr, uint32_t columns) {
+  asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(columns)
+               : "memory");
+}
+
+__device__ __forceinline__ void tc_fence_before() {
+  asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+}
+__device__ __forceinline__ void tc_fence_after() {
+  asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+}
+
+__device__ __forceinline__ void mma_bf16(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc,
+                                         uint32_t idesc, uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(tmem_d),
+      "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+
+__device__ __forceinline__ void mma_commit(uint64_t* bar) {
+  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
+                   shared_address(bar))
+               : "memory");
+}
+
+// 32 consecutive fp32 accumulator columns of this thread's TMEM lane.
+__device__ __forceinline__ void tmem_load32(uint32_t taddr, uint32_t* v) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x32.b32 "
+      "{%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15, "
+      "%16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31}, [%32];"
+      : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3]), "=r"(v[4]), "=r"(v[5]), "=r"(v[6]),
+        "=r"(v[7]), "=r"(v[8]), "=r"(v[9]), "=r"(v[10]), "=r"(v[11]), "=r"(v[12]), "=r"(v[13]),
+        "=r"(v[14]), "=r"(v[15]), "=r"(v[16]), "=r"(v[17]), "=r"(v[18]), "=r"(v[19]),
+        "=r"(v[20]), "=r"(v[21]), "=r"(v[22]), "=r"(v[23]), "=r"(v[24]), "=r"(v[25]),
+        "=r"(v[26]), "=r"(v[27]), "=r"(v[28]), "=r"(v[29]), "=r"(v[30]), "=r"(v[31])
+      : "r"(taddr));
+  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+}
+
+// Shared-memory matrix descriptor of a K-major, 128-byte-swizzled tile whose
+// rows are 128 bytes and whose 8-row groups are 1024 bytes apart (the layout
+// the TMA engine writes for a 64-element bf16 box with SWIZZLE_128B): start
+// address >> 4 in bits [0, 14), leading offset 1 (unused for this layout) in
+// [16, 30), stride offset 1024 >> 4 in [32, 46), descriptor version 1 at
+// bit 46, layout 2 (128-byte swizzle) in [61, 64).
+__device__ __forceinline__ uint64_t smem_descriptor(const void* tile) {
+  const uint64_t address = shared_address(tile);
+  return ((address & 0x3FFFFull) >> 4) | (uint64_t{1} << 16) | (uint64_t{1024 >> 4} << 32) |
+         (uint64_t{1} << 46) | (uint64_t{2} << 61);
+}
+
+__device__ __forceinline__ bool wait_or_record(uint64_t* bar, uint32_t parity) {
+  if (mbarrier_wait_bounded(bar, parity)) return true;
+  atomicAdd(&g_gemm_expired_waits, 1u);
+  return false;
+}
+
+// bf16 pair word of two fp32 accumulators (round to nearest even).
+__device__ __forceinline__ uint32_t round_pair(uint32_t lo, uint32_t hi) {
+  return Pack<__nv_bfloat16>::f32_to_word(__uint_as_float(lo), __uint_as_float(hi));
+}
+
+// One 128-wide head of this thread's row, rounded to bf16: 64 words, word i
+// holding elements 2i and 2i + 1.
+__device__ __forceinline__ void load_head(uint32_t taddr, uint32_t* words) {
+#pragma unroll
+  for (int chunk = 0; chunk < 4; ++chunk) {
+    uint32_t acc[32];
+    tmem_load32(taddr + chunk * 32, acc);
+#pragma unroll
+    for (int i = 0; i < 16; ++i) words[chunk * 16 + i] = round_pair(acc[2 * i], acc[2 * i + 1]);
+  }
+}
+
+__device__ __forceinline__ Half8<__nv_bfloat16> chunk_of(const uint32_t* words, int element) {
+  Half8<__nv_bfloat16> h;
+#pragma unroll
+  for (int i = 0; i < 4; ++i) h.w[i] = words[element / 2 + i];
+  return h;
+}
+
+__device__ __forceinline__ void put_chunk(uint32_t* words, int element,
+                                          const Half8<__nv_bfloat16>& h) {
+#pragma unroll
+  for (int i = 0; i < 4; ++i) words[element / 2 + i] = h.w[i];
+}
+
+__device__ __forceinline__ void store_head(__nv_bfloat16* dst, const uint32_t* words) {
+#pragma unroll
+  for (int i = 0; i < 16; ++i) {
+    store16(dst + 8 * i, make_uint4(words[4 * i], words[4 * i + 1], words[4 * i + 2],
+                                    words[4 * i + 3]));
+  }
+}
+
+// Per-head RMSNorm + RoPE of one row in place, bit-identical to
+// head_norm_rope_kernel: lane slice j of that kernel holds elements
+// [8j, 8j + 8) and [64 + 8j, 64 + 8j + 8); its sum of squares is formed per
+// slice (even / odd accumulators) and combined by the butterfly 4, 2, 1.
+__device__ __forceinline__ void norm_rope_head(uint32_t* words, const __nv_bfloat16* weight,
+                                               const float* cos_sin_row, float epsilon) {
+  float slice[8];
+#pragma unroll
+  for (int j = 0; j < 8; ++j) {
+    const float2 acc = half_sum_squares<__nv_bfloat16>(
+        chunk_of(words, 64 + 8 * j),
+        half_sum_squares<__nv_bfloat16>(chunk_of(words, 8 * j), make_float2(0.f, 0.f)));
+    slice[j] = __fadd_rn(acc.x, acc.y);
+  }
+  float t[4];
+#pragma unroll
+  for (int j = 0; j < 4; ++j) t[j] = __fadd_rn(slice[j], slice[j + 4]);
+  const float total = __fadd_rn(__fadd_rn(t[0], t[2]), __fadd_rn(t[1], t[3]));
+  const float inv = head_inverse_rms<kHead>(make_float2(total, 0.0f), epsilon);
+#pragma unroll
+  for (int j = 0; j < 8; ++j) {
+    const int lo = 8 * j, hi = 64 + 8 * j;
+    const Half8<__nv_bfloat16> n_lo =
+        normalise_half<__nv_bfloat16>(chunk_of(words, lo), load_half<__nv_bfloat16, true>(weight + lo), inv);
+    const Half8<__nv_bfloat16> n_hi =
+        normalise_half<__nv_bfloat16>(chunk_of(words, hi), load_half<__nv_bfloat16, true>(weight + hi), inv);
+    float2 c[4], s[4];
+    load8_pairs<true>(cos_sin_row + lo, c);
+    load8_pairs<true>(cos_sin_row + hi, s);
+    Half8<__nv_bfloat16> y_lo, y_hi;
+    rotate_half<__nv_bfloat16>(n_lo, n_hi, c, s, y_lo, y_hi);
+    put_chunk(words, lo, y_lo);
+    put_chunk(words, hi, y_hi);
+  }
+}
+
+template <int kTileN, int kStages, int kWarps>
+__global__ void __launch_bounds__(kWarps * kWarpSize, 1)
+    qkv_gemm_kernel(const __grid_constant__ CUtensorMap map_a,
+                    const __grid_constant__ CUtensorMap map_b, GemmArgs a) {
+  using S = Shape<kTileN, kStages, kWarps>;
+  extern __shared__ unsigned char dynamic_smem[];
+  __shared__ __align__(8) uint64_t full[kStages];
+  __shared__ __align__(8) uint64_t empty[kStages];
+  __shared__ __align__(8) uint64_t done;
+  __shared__ uint32_t tmem_slot;
+  __shared__ int aborted;
+  // 128-byte swizzled tiles need 1024-byte-aligned stages
+  unsigned char* tiles = reinterpret_cast<unsigned char*>(
+      (reinterpret_cast<uintptr_t>(dynamic_smem) + 1023) & ~uintptr_t{1023});
+  const int warp = threadIdx.x / kWarpSize;
+  const int lane = threadIdx.x & (kWarpSize - 1);
+  const int n_tile = blockIdx.x;
+  const int m_tile = blockIdx.y;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < kStages; ++s) {
+      mbarrier_init(&full[s], 1);
+      mbarrier_init(&empty[s], 1);
+    }
+    mbarrier_init(&done, 1);
+    aborted = 0;
+    fence_mbarrier_init();
+  }
+  if (warp == 0) tmem_alloc(&tmem_slot, S::kTmemColumns);
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = tmem_slot;
+  wait_for_upstream_grid();
+  release_downstream_grid();
+
+  if (warp == 0 && lane == 0) {
+    // loader
+    for (int k = 0; k < a.k_tiles; ++k) {
+      const int s = k % kStages;
+      if (k >= kStages && !wait_or_record(&empty[s], ((k / kStages) - 1) & 1)) {
+        atomicExch(&aborted, 1);
+        break;
+      }
+      if (atomicAdd(&aborted, 0)) break;
+      unsigned char* stage = tiles + static_cast<size_t>(s) * S::kStageBytes;
+      mbarrier_arrive_expect_tx(&full[s], S::kStageBytes);
+      tma_load_2d(stage, &map_a, k * kTileK, m_tile * kTileM, &full[s]);
+      tma_load_2d(stage + kABytes, &map_b, k * kTileK, n_tile * kTileN, &full[s]);
+    }
+  } else if (warp == 1 && lane == 0) {
+    // tensor-core issuer
+    int k = 0;
+    for (; k < a.k_tiles; ++k) {
+      const int s = k % kStages;
+      if (!wait_or_record(&full[s], (k / kStages) & 1)) {
+        atomicExch(&aborted, 1);
+        break;
+      }
+      tc_fence_after();
+      const unsigned char* stage = tiles + static_cast<size_t>(s) * S::kStageBytes;
+      const uint64_t adesc = smem_descriptor(stage);
+      const uint64_t bdesc = smem_descriptor(stage + kABytes);
+#pragma unroll
+      for (int kk = 0; kk < kTileK / kMmaK; ++kk) {
+        // advance 16 elements (32 bytes, 2 descriptor units) along K
+        mma_bf16(tmem_base, adesc + 2 * kk, bdesc + 2 * kk, S::kInstrDesc, (k | kk) != 0);
+      }
+      mma_commit(&empty[s]);
+    }
+    mma_commit(&done);  // fires once every MMA issued above has completed
+  }
+  __syncwarp();
+
+  // ---- epilogue: every warp; warp w reads TMEM lanes 32 * (w % 4) onwards
+  // and the heads hh with hh % (kWarps / 4) == w / 4 ----
+  const bool ready = wait_or_record(&done, 0);
+  tc_fence_after();
+  const int lane_group = warp % 4;
+  const int head_group = warp / 4;
+  const int64_t row = static_cast<int64_t>(m_tile) * kTileM + lane_group * 32 + lane;
+  if (ready && !aborted) {
+    const bool live = row < a.tokens;
+    int64_t position = -1;
+    int64_t slot = -1;
+    if (live && a.epilogue) {
+      position = a.positions[row];
+      slot = a.slots != nullptr ? a.slots[row] : -1;
+      if (slot >= a.cache_slots) slot = -1;
+    }
+    const bool rope = position >= 0 && position < a.rope_positions;
+#pragma unroll 1
+    for (int hh = head_group; hh < S::kHeads; hh += kWarps / 4) {
+      uint32_t words[64];
+      load_head(tmem_base + (static_cast<uint32_t>(lane_group * 32) << 16) + hh * kHead, words);
+      if (!live) continue;  // after the warp-wide TMEM load
+      const int head = n_tile * S::kHeads + hh;
+      __nv_bfloat16* out = a.qkv + row * a.n + static_cast<int64_t>(head) * kHead;
+      if (a.epilogue && rope && head < a.query_heads + a.key_heads) {
+        const bool is_query = head < a.query_heads;
+        norm_rope_head(words, is_query ? a.query_weight : a.key_weight,
+                       a.cos_sin + position * kHead, a.epsilon);
+      }
+      store_head(out, words);
+      if (a.epilogue && rope && slot >= 0 && head >= a.query_heads) {
+        const bool is_key = head < a.query_heads + a.key_heads;
+        const int kv_head = is_key ? head - a.query_heads : head - a.query_heads - a.key_heads;
+        __nv_bfloat16* cache = is_key ? a.key_cache : a.value_cache;
+        store_head(cache + (slot * a.key_heads + kv_head) * kHead, words);
+      }
+    }
+  }
+  // release tensor memory once every warp is past its loads; after an expired
+  // wait, first give in-flight tensor-core work a bounded chance to finish
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 0) {
+    if (!ready) {
+      if (lane == 0) mbarrier_wait_bounded(&done, 0);
+      __syncwarp();
+    }
+    tc_fence_after();
+    tmem_dealloc(tmem_base, S::kTmemColumns);
+  }
+}
+
+// ---- host ----------------------------------------------------------------
+PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder(int* rc) {
+  static std::once_flag once;
+  static PFN_cuTensorMapEncodeTiled_v12000 encode = nullptr;
+  static cudaError_t status = cudaSuccess;
+  std::call_once(once, [] {
+    cudaDriverEntryPointQueryResult query;
+    status = cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", reinterpret_cast<void**>(&encode),
+                                     cudaEnableDefault, &query);
+    if (status == cudaSuccess && query != cudaDriverEntryPointSuccess) status = cudaErrorNotSupported;
+  });
+  *rc = status == cudaSuccess && encode != nullptr
+            ? SM120N_OK
+            : fail(SM120N_ERR_CUDA, "cuTensorMapEncodeTiled is not available: %s",
+                   cudaGetErrorString(status));
+  return encode;
+}
+
+// Row-major [rows, cols] bf16 matrix as a TMA map with a 64 x box_rows box,
+// 128-byte swizzle; rows past the end read as zeros.
+int make_map(CUtensorMap* map, const void* base, int64_t rows, int64_t cols, int box_rows) {
+  int rc = SM120N_OK;
+  auto encode = tensor_map_encoder(&rc);
+  if (rc != SM120N_OK) return rc;
+  const cuuint64_t dims[2] = {static_cast<cuuint64_t>(cols), static_cast<cuuint64_t>(rows)};
+  const cuuint64_t strides[1] = {static_cast<cuuint64_t>(cols) * 2};
+  const cuuint32_t box[2] = {static_cast<cuuint32_t>(kTileK), static_cast<cuuint32_t>(box_rows)};
+  const cuuint32_t element_strides[2] = {1, 1};
+  const CUresult r = encode(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(base), dims,
+                            strides, box, element_strides, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                            CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                            CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) {
+    return fail(SM120N_ERR_CUDA, "cuTensorMapEncodeTiled failed (%d)", static_cast<int>(r));
+  }
+  return SM120N_OK;
+}
+
+template <int kTileN, int kStages, int kWarps>
+int launch_gemm(const CUtensorMap& map_a, const void* qkv_weight, int64_t n, int64_t hidden_size,
+                const GemmArgs& a, int64_t tokens, cudaStream_t stream) {
+  using S = Shape<kTileN, kStages, kWarps>;
+  CUtensorMap map_b;
+  int rc = make_map(&map_b, qkv_weight, n, hidden_size, kTileN);
+  if (rc != SM120N_OK) return rc;
+  auto kernel = qkv_gemm_kernel<kTileN, kStages, kWarps>;
+  rc = allow_dynamic_smem(reinterpret_cast<const void*>(kernel), S::kSmem);
+  if (rc != SM120N_OK) return rc;
+  const dim3 grid(static_cast<unsigned>(n / kTileN),
+                  static_cast<unsigned>((tokens + kTileM - 1) / kTileM));
+  return launch(kernel, grid, dim3(S::kThreads), S::kSmem, stream, map_a, map_b, a);
+}
+
+}  // namespace
+
+int read_gemm_faults(unsigned int* value) {
+  const cudaError_t err = cudaMemcpyFromSymbol(value, g_gemm_expired_waits, sizeof *value);
+  return err == cudaSuccess ? SM120N_OK
+                            : fail(SM120N_ERR_CUDA, "reading the fault counter failed: %s",
+                                   cudaGetErrorString(err));
+}
+
+int reset_gemm_faults() {
+  const unsigned int zero = 0;
+  const cudaError_t err = cudaMemcpyToSymbol(g_gemm_expired_waits, &zero, sizeof zero);
+  return err == cudaSuccess ? SM120N_OK
+                            : fail(SM120N_ERR_CUDA, "resetting the fault counter failed: %s",
+                                   cudaGetErrorString(err));
+}
+
+}  // namespace sm120n
+
+using namespace sm120n;
+
+extern "C" int sm120n_qkv_proj_norm_rope_cache(
+    const void* hidden, const void* qkv_weight, void* qkv, int64_t tokens, int64_t hidden_size,
+    int64_t query_heads, int64_t key_heads, const void* query_weight, const void* key_weight,
+    const int64_t* positions, const float* cos_sin_cache, int64_t rope_positions,
+    void* key_cache, void* value_cache, const int32_t* slot_mapping, int64_t cache_slots,
+    float epsilon, int epilogue, void* stream) {
+  clear_error();
+  if (tokens < 0 || query_heads < 0 || key_heads < 0 || rope_positions < 0 || cache_slots < 0) {
+    return fail(SM120N_ERR_INVALID_ARGUMENT, "sizes must be non-negative");
+  }
+  if (epilogue != 0 && epilogue != 1) {
+    return fail(SM120N_ERR_INVALID_ARGUMENT, "epilogue must be 0 (GEMM only) or 1");
+  }
+  const int64_t heads = query_heads + 2 * key_heads;
+  if (heads <= 0 || heads % 2 != 0 || heads > 4096) {
+    return fail(SM120N_ERR_UNSUPPORTED,
+                "the fused projection needs an even number of heads (query + 2 * key), "
+                "at most 4096 (got %lld)", static_cast<long long>(heads));
+  }
+  if (hidden_size <= 0 || hidden_size % kTileK != 0 || hidden_size > (int64_t{1} << 20)) {
+    return fail(SM120N_ERR_UNSUPPORTED,
+                "hidden_size must be a positive multiple of 64 up to 2^20 (got %lld)",
+                static_cast<long long>(hidden_size));
+  }
+  if (tokens > INT32_MAX - kTileM) return fail(SM120N_ERR_INVALID_ARGUMENT, "too many tokens");
+  if (tokens == 0) return SM120N_OK;
+  if (!hidden || !qkv_weight || !qkv) {
+    return fail(SM120N_ERR_INVALID_ARGUMENT, "hidden, qkv_weight and qkv must be non-null");
+  }
+  if (epilogue && (!query_weight || !key_weight || !positions || !cos_sin_cache)) {
+    return fail(SM120N_ERR_INVALID_ARGUMENT,
+                "the norm epilogue needs query/key weights, positions and the cos/sin cache");
+  }
+  if (epilogue && key_heads > 0 && slot_mapping &&
+      (cache_slots > 0 && (!key_cache || !value_cache))) {
+    return fail(SM120N_ERR_INVALID_ARGUMENT, "a KV store needs key_cache and value_cache");
+  }
+  if (!aligned16(hidden) || !aligned16(qkv_weight) || !aligned16(qkv) ||
+      (epilogue && (!aligned16(query_weight) || !aligned16(key_weight) ||
+                    !aligned16(cos_sin_cache) || (key_cache && !aligned16(key_cache)) ||
+                    (value_cache && !aligned16(value_cache))))) {
+    return fail(SM120N_ERR_UNSUPPORTED, "the fused projection needs 16-byte-aligned buffers");
+  }
+  const int64_t n = heads * kHead;
+  CUtensorMap map_a;
+  int rc = make_map(&map_a, hidden, tokens, hidden_size, kTileM);
+  if (rc != SM120N_OK) return rc;
+  GemmArgs a{static_cast<__nv_bfloat16*>(qkv),
+             static_cast<const __nv_bfloat16*>(query_weight),
+             static_cast<const __nv_bfloat16*>(key_weight),
+             positions,
+             cos_sin_cache,
+             static_cast<__nv_bfloat16*>(key_cache),
+             static_cast<__nv_bfloat16*>(value_cache),
+             epilogue ? slot_mapping : nullptr,
+             tokens,
+             rope_positions,
+             (key_cache && value_cache) ? cache_slots : 0,
+             static_cast<int>(hidden_size / kTileK),
+             static_cast<int>(query_heads),
+             static_cast<int>(key_heads),
+             static_cast<int>(n),
+             epsilon,
+             epilogue};
+  const cudaStream_t st = static_cast<cudaStream_t>(stream);
+  // Measured on B200 (Qwen3-8B-shaped projection, N = 6144, K = 4096): one
+  // head per block and six stages for up to 256 tokens (33 us at 1 token,
+  // against 37 us with two heads per block), two heads per block and four
+  // stages above (1360 us at 32768 tokens, against 2296 us with one head);
+  // two blocks per SM or eight warps per block were slower everywhere.
+  if (tokens <= 256) return launch_gemm<128, 6, 4>(map_a, qkv_weight, n, hidden_size, a, tokens, st);
+  return launch_gemm<256, 4, 4>(map_a, qkv_weight, n, hidden_size, a, tokens, st);
+}

@@ -608,7 +608,10 @@ extern "C" int sm120n_get_device_faults(uint32_t* out_count) {
   if (err != cudaSuccess) {
     return fail(SM120N_ERR_CUDA, "reading the fault counter failed: %s", cudaGetErrorString(err));
   }
-  *out_count = value;
+  unsigned int gemm = 0;
+  const int rc = read_gemm_faults(&gemm);
+  if (rc != SM120N_OK) return rc;
+  *out_count = value + gemm;
   return SM120N_OK;
 }
 
@@ -619,5 +622,5 @@ extern "C" int sm120n_reset_device_faults(void) {
   if (err != cudaSuccess) {
     return fail(SM120N_ERR_CUDA, "resetting the fault counter failed: %s", cudaGetErrorString(err));
   }
-  return SM120N_OK;
+  return reset_gemm_faults();
 }

@@ -65,6 +65,11 @@ int launch(void (*kernel)(KernelArgs...), dim3 grid, dim3 block, size_t smem,
   return SM120N_OK;
 }
 
+// Expired-wait counter of the tensor-core projection kernel (qkv_gemm.cu),
+// read / reset alongside the row kernels' counter.
+int read_gemm_faults(unsigned int* value);
+int reset_gemm_faults();
+
 // Element size of an sm120n_dtype code, or 0 for an unknown code.
 inline int dtype_size(int dtype) {
   switch (dtype) {

@@ -494,6 +494,86 @@ void b200_rms_norm_nvfp4_quant(torch::Tensor result, torch::Tensor block_scale,
       swizzled_scales ? SM120N_SCALES_TILED_128X4 : SM120N_SCALES_ROW_MAJOR, current_stream()));
 }
 
+// QKV projection (tensor cores) with the Q/K norm + RoPE + KV store fused
+// into the epilogue (fuse_norm) or as a plain GEMM.
+void b200_qkv_proj_norm_rope_cache(torch::Tensor hidden, torch::Tensor qkv_weight,
+                                   torch::Tensor qkv, int64_t query_heads, int64_t key_heads,
+                                   c10::optional<torch::Tensor> query_weight,
+                                   c10::optional<torch::Tensor> key_weight,
+                                   c10::optional<torch::Tensor> positions,
+                                   c10::optional<torch::Tensor> cos_sin_cache,
+                                   c10::optional<torch::Tensor> key_cache,
+                                   c10::optional<torch::Tensor> value_cache,
+                                   c10::optional<torch::Tensor> slot_mapping, double epsilon,
+                                   bool fuse_norm) {
+  for (const auto* t : {&hidden, &qkv_weight, &qkv}) {
+    TORCH_CHECK(t->is_cuda() && t->is_contiguous() && t->scalar_type() == torch::kBFloat16 &&
+                    t->dim() == 2 && t->device() == hidden.device(),
+                "hidden, qkv_weight and qkv must be contiguous 2-D bf16 CUDA tensors on one device");
+  }
+  const int64_t n = (query_heads + 2 * key_heads) * 128;
+  TORCH_CHECK(qkv_weight.size(0) == n && qkv_weight.size(1) == hidden.size(1),
+              "qkv_weight must be [(query_heads + 2 * key_heads) * 128, hidden_size]");
+  TORCH_CHECK(qkv.size(0) == hidden.size(0) && qkv.size(1) == n,
+              "qkv must be [tokens, (query_heads + 2 * key_heads) * 128]");
+  const void* qw = nullptr;
+  const void* kw = nullptr;
+  const int64_t* pos = nullptr;
+  const float* table = nullptr;
+  int64_t rope_positions = 0;
+  void* kc = nullptr;
+  void* vc = nullptr;
+  const int32_t* slots = nullptr;
+  int64_t cache_slots = 0;
+  if (fuse_norm) {
+    TORCH_CHECK(query_weight.has_value() && key_weight.has_value() && positions.has_value() &&
+                    cos_sin_cache.has_value(),
+                "the fused norm needs query_weight, key_weight, positions and cos_sin_cache");
+    TORCH_CHECK(query_weight->is_cuda() && key_weight->is_cuda() &&
+                    query_weight->scalar_type() == torch::kBFloat16 &&
+                    key_weight->scalar_type() == torch::kBFloat16 &&
+                    query_weight->numel() == 128 && key_weight->numel() == 128 &&
+                    query_weight->is_contiguous() && key_weight->is_contiguous(),
+                "Q/K weights must be contiguous bf16 CUDA tensors of 128 elements");
+    TORCH_CHECK(positions->is_cuda() && positions->is_contiguous() &&
+                    positions->scalar_type() == torch::kInt64 &&
+                    positions->numel() == hidden.size(0),
+                "positions must be contiguous CUDA int64 with one entry per token");
+    TORCH_CHECK(cos_sin_cache->is_cuda() && cos_sin_cache->is_contiguous() &&
+                    cos_sin_cache->scalar_type() == torch::kFloat32 &&
+                    cos_sin_cache->size(-1) == 128,
+                "cos/sin cache must be contiguous CUDA float32 with last dimension 128");
+    qw = query_weight->data_ptr();
+    kw = key_weight->data_ptr();
+    pos = positions->data_ptr<int64_t>();
+    table = cos_sin_cache->data_ptr<float>();
+    rope_positions = cos_sin_cache->numel() / 128;
+    if (key_cache.has_value() || value_cache.has_value()) {
+      TORCH_CHECK(key_cache.has_value() && value_cache.has_value() && slot_mapping.has_value(),
+                  "a KV store needs key_cache, value_cache and slot_mapping");
+      TORCH_CHECK(key_cache->is_cuda() && value_cache->is_cuda() && key_cache->is_contiguous() &&
+                      value_cache->is_contiguous() &&
+                      key_cache->scalar_type() == torch::kBFloat16 &&
+                      key_cache->sizes() == value_cache->sizes() && key_cache->dim() >= 2 &&
+                      key_cache->size(-2) == key_heads && key_cache->size(-1) == 128,
+                  "KV caches must be contiguous bf16 CUDA tensors ending in [key_heads, 128]");
+      TORCH_CHECK(slot_mapping->is_cuda() && slot_mapping->is_contiguous() &&
+                      slot_mapping->scalar_type() == torch::kInt &&
+                      slot_mapping->numel() == hidden.size(0),
+                  "slot_mapping must be contiguous CUDA int32 with one entry per token");
+      kc = key_cache->data_ptr();
+      vc = value_cache->data_ptr();
+      slots = slot_mapping->data_ptr<int32_t>();
+      cache_slots = key_heads == 0 ? 0 : key_cache->numel() / (key_heads * 128);
+    }
+  }
+  c10::cuda::CUDAGuard guard(hidden.device());
+  raise_if_failed(sm120n_qkv_proj_norm_rope_cache(
+      hidden.data_ptr(), qkv_weight.data_ptr(), qkv.data_ptr(), hidden.size(0), hidden.size(1),
+      query_heads, key_heads, qw, kw, pos, table, rope_positions, kc, vc, slots, cache_slots,
+      static_cast<float>(epsilon), fuse_norm ? 1 : 0, current_stream()));
+}
+
 TORCH_LIBRARY(sm120_norm_ext, m) {
   m.def(
       "qk_norm_rope_cache_(Tensor(a!) query, Tensor(b!) key, Tensor? value, "
@@ -514,6 +594,12 @@ TORCH_LIBRARY(sm120_norm_ext, m) {
       "rms_norm_nvfp4_quant(Tensor(a!) result, Tensor(b!) block_scale, Tensor input, "
       "Tensor weight, Tensor global_scale, float epsilon=1e-6, Tensor(c!)? residual=None, "
       "bool swizzled_scales=True) -> ()");
+  m.def(
+      "qkv_proj_norm_rope_cache_(Tensor hidden, Tensor qkv_weight, Tensor(a!) qkv, "
+      "int query_heads, int key_heads, Tensor? query_weight=None, Tensor? key_weight=None, "
+      "Tensor? positions=None, Tensor? cos_sin_cache=None, Tensor(b!)? key_cache=None, "
+      "Tensor(c!)? value_cache=None, Tensor? slot_mapping=None, float epsilon=1e-6, "
+      "bool fuse_norm=True) -> ()");
 }
 
 TORCH_LIBRARY_IMPL(sm120_norm_ext, CUDA, m) {
@@ -522,6 +608,7 @@ TORCH_LIBRARY_IMPL(sm120_norm_ext, CUDA, m) {
   m.impl("fused_add_rms_norm_static_fp8_quant", &b200_fused_add_rms_norm_static_fp8_quant);
   m.impl("rms_norm_dynamic_per_token_quant", &b200_rms_norm_dynamic_per_token_quant);
   m.impl("rms_norm_nvfp4_quant", &b200_rms_norm_nvfp4_quant);
+  m.impl("qkv_proj_norm_rope_cache_", &b200_qkv_proj_norm_rope_cache);
 }
 
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {

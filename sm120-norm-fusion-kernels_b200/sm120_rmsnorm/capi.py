@@ -86,6 +86,9 @@ SIGNATURES: dict[str, tuple[list, object]] = {
         [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _i64, _i64, _i32, _f32, _vp], _i32),
     "sm120n_rms_norm_fp4_quant": (
         [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _i64, _i64, _i32, _f32, _i32, _vp], _i32),
+    "sm120n_qkv_proj_norm_rope_cache": (
+        [_vp, _vp, _vp, _i64, _i64, _i64, _i64, _vp, _vp, _vp, _vp, _i64, _vp, _vp, _vp, _i64,
+         _f32, _i32, _vp], _i32),
 }
 
 
@@ -191,3 +194,18 @@ def rms_norm_fp4_quant(input_ptr, residual_ptr, weight_ptr, residual_output_ptr,
     _check(load().sm120n_rms_norm_fp4_quant(
         input_ptr, residual_ptr, weight_ptr, residual_output_ptr, output_ptr, block_scales_ptr,
         global_scale_ptr, rows, hidden_size, dtype, epsilon, scale_layout, stream))
+
+
+def qkv_proj_norm_rope_cache(hidden_ptr, qkv_weight_ptr, qkv_ptr, tokens, hidden_size,
+                             query_heads, key_heads, query_weight_ptr=None, key_weight_ptr=None,
+                             positions_ptr=None, cos_sin_ptr=None, rope_positions=0,
+                             key_cache_ptr=None, value_cache_ptr=None, slot_mapping_ptr=None,
+                             cache_slots=0, epsilon=1e-6, epilogue=1, stream=0) -> None:
+    """QKV projection on the tensor cores with the Q/K norm + RoPE + KV store
+    in its epilogue (epilogue=1) or as a plain GEMM (epilogue=0)
+    (sm120n_qkv_proj_norm_rope_cache)."""
+    _check(load().sm120n_qkv_proj_norm_rope_cache(
+        hidden_ptr, qkv_weight_ptr, qkv_ptr, tokens, hidden_size, query_heads, key_heads,
+        query_weight_ptr, key_weight_ptr, positions_ptr, cos_sin_ptr, rope_positions,
+        key_cache_ptr, value_cache_ptr, slot_mapping_ptr, cache_slots, epsilon, epilogue,
+        stream))

@@ -13,6 +13,11 @@ are called from a decode engine's Qwen3 layer):
    (the reference's kernel needs contiguous Q / K, so an engine built on it
    copies them out first).
 
+With ``fused_projection=True`` steps 2 and 3 are one kernel: the QKV
+projection on the tensor cores with the Q/K norm + RoPE + KV store in its
+epilogue (``extensions.qkv_proj_norm_rope_cache_``; bf16, head_dim 128, dense
+NHD caches), bit-identical to that kernel's plain GEMM followed by step 3.
+
 :class:`DecodeGraph` captures the prologues of all layers of one decode step
 into a single CUDA graph, so the host launches one graph per step; the B200
 kernels additionally overlap each launch with the tail of the previous kernel
@@ -82,9 +87,15 @@ class Qwen3AttentionPrologue:
     def forward(self, hidden: torch.Tensor, residual: torch.Tensor, positions: torch.Tensor,
                 cos_sin_cache: torch.Tensor, key_cache: torch.Tensor, value_cache: torch.Tensor,
                 slot_mapping: torch.Tensor, qkv_out: torch.Tensor, k_scale=None, v_scale=None,
-                kv_cache_layout: str = "NHD"):
+                kv_cache_layout: str = "NHD", fused_projection: bool = False):
         s = self.shape
         ops.fused_add_rms_norm_inplace(hidden, residual, self.input_norm_weight, s.epsilon)
+        if fused_projection:
+            extensions.qkv_proj_norm_rope_cache_(
+                hidden, self.qkv_weight, qkv_out, s.query_heads, s.key_heads,
+                self.query_norm_weight, self.key_norm_weight, positions, cos_sin_cache,
+                key_cache, value_cache, slot_mapping, s.epsilon)
+            return self.split(qkv_out)
         torch.matmul(hidden, self.qkv_weight.t(), out=qkv_out)
         q, k, v = self.split(qkv_out)
         extensions.qk_norm_rope_cache_(
@@ -107,7 +118,8 @@ class DecodeGraph:
 
     def __init__(self, layers: list[Qwen3AttentionPrologue], batch: int, cos_sin_cache,
                  key_caches: list[torch.Tensor], value_caches: list[torch.Tensor],
-                 k_scale=None, v_scale=None, kv_cache_layout: str = "NHD"):
+                 k_scale=None, v_scale=None, kv_cache_layout: str = "NHD",
+                 fused_projection: bool = False):
         shape = layers[0].shape
         if shape.qkv_width < shape.hidden:
             raise ValueError("the stand-in between layers needs qkv_width >= hidden")
@@ -120,7 +132,8 @@ class DecodeGraph:
         self.slot_mapping = torch.full((batch,), -1, device=dev, dtype=torch.int32)
         self.qkv = [torch.empty(batch, shape.qkv_width, device=dev, dtype=dtype) for _ in layers]
         self.layer_hidden = [torch.empty_like(self.hidden) for _ in layers[1:]]
-        self._args = (cos_sin_cache, key_caches, value_caches, k_scale, v_scale, kv_cache_layout)
+        self._args = (cos_sin_cache, key_caches, value_caches, k_scale, v_scale, kv_cache_layout,
+                      fused_projection)
         self._run()  # load kernels and pick cuBLAS algorithms before capture
         torch.cuda.synchronize()
         self.graph = torch.cuda.CUDAGraph()
@@ -128,12 +141,12 @@ class DecodeGraph:
             self._run()
 
     def _run(self):
-        cos_sin, key_caches, value_caches, k_scale, v_scale, layout = self._args
+        cos_sin, key_caches, value_caches, k_scale, v_scale, layout, fused = self._args
         hidden = self.hidden
         for i, layer in enumerate(self.layers):
             layer.forward(hidden, self.residual, self.positions, cos_sin, key_caches[i],
                           value_caches[i], self.slot_mapping, self.qkv[i], k_scale, v_scale,
-                          layout)
+                          layout, fused)
             if i + 1 < len(self.layers):
                 nxt = self.layer_hidden[i]
                 nxt.copy_(self.qkv[i][:, :layer.shape.hidden])

@@ -116,6 +116,28 @@ def rms_norm_nvfp4_quant(result: torch.Tensor, block_scale: torch.Tensor, input:
                                                   swizzled_scales)
 
 
+def qkv_proj_norm_rope_cache_(hidden: torch.Tensor, qkv_weight: torch.Tensor,
+                              qkv: torch.Tensor, query_heads: int, key_heads: int,
+                              query_weight: torch.Tensor | None = None,
+                              key_weight: torch.Tensor | None = None,
+                              positions: torch.Tensor | None = None,
+                              cos_sin_cache: torch.Tensor | None = None,
+                              key_cache: torch.Tensor | None = None,
+                              value_cache: torch.Tensor | None = None,
+                              slot_mapping: torch.Tensor | None = None,
+                              epsilon: float = 1e-6, fuse_norm: bool = True) -> None:
+    """``qkv = hidden @ qkv_weight.T`` on the tensor cores (bf16, fp32
+    accumulation) into ``qkv`` ``[tokens, (Hq + 2Hk) * 128]``; with
+    ``fuse_norm`` the epilogue then applies, per head, exactly what
+    ``ops.fused_qk_rms_norm_rope_kv`` does to the ``[tokens, heads, 128]`` view
+    of ``qkv`` (Q/K norm + RoPE in place, rotated K and V into the caches at
+    ``slot_mapping`` when caches are given)."""
+    _extension()
+    torch.ops.sm120_norm_ext.qkv_proj_norm_rope_cache_(
+        hidden, qkv_weight, qkv, query_heads, key_heads, query_weight, key_weight, positions,
+        cos_sin_cache, key_cache, value_cache, slot_mapping, epsilon, fuse_norm)
+
+
 def nvfp4_scale_bytes(rows: int, hidden: int, swizzled_scales: bool = True) -> int:
     """Bytes of the block-scale buffer for ``rows`` x ``hidden``."""
     blocks = hidden // 16
@@ -151,4 +173,11 @@ if _C is not None:
     @torch.library.register_fake("sm120_norm_ext::rms_norm_nvfp4_quant")
     def _rms_norm_nvfp4_quant_meta(result, block_scale, input, weight, global_scale,
                                    epsilon=1e-6, residual=None, swizzled_scales=True) -> None:
+        return None
+
+    @torch.library.register_fake("sm120_norm_ext::qkv_proj_norm_rope_cache_")
+    def _qkv_proj_norm_rope_cache_meta(hidden, qkv_weight, qkv, query_heads, key_heads,
+                                       query_weight=None, key_weight=None, positions=None,
+                                       cos_sin_cache=None, key_cache=None, value_cache=None,
+                                       slot_mapping=None, epsilon=1e-6, fuse_norm=True) -> None:
         return None

@@ -22,11 +22,11 @@ def header_symbols() -> set[str]:
 def test_library_loads_and_exports_every_declared_symbol():
     lib = capi.load()
     declared = header_symbols()
-    assert len(declared) == 14, declared
+    assert len(declared) == 15, declared
     for name in declared:
         assert hasattr(lib, name), name
     assert declared == set(capi.SIGNATURES), "capi.SIGNATURES must bind exactly the header"
-    assert capi.abi_version() == 3
+    assert capi.abi_version() == 4
 
 
 def test_library_exports_nothing_else():
