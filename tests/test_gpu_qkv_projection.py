@@ -52,7 +52,7 @@ def test_plain_gemm_is_exact_on_exact_inputs(tokens, hidden, hq, hk):
     assert_bitwise_equal(out, a @ w.t(), what="GEMM")
 
 
-@pytest.mark.parametrize("tokens, hidden", [(64, 4096), (513, 1024)])
+@pytest.mark.parametrize("tokens, hidden", [(1, 4096), (2, 4096), (64, 4096), (513, 1024)])
 def test_plain_gemm_random_inputs_within_one_ulp(tokens, hidden):
     a, w = operands(tokens, hidden, 32, 8, 5, exact=False)
     out = torch.empty(tokens, w.shape[0], device=DEV, dtype=torch.bfloat16)
