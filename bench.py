@@ -1097,6 +1097,19 @@ def profile_case(args) -> None:
         out = torch.empty(t, h, device="cuda", dtype=torch.float8_e4m3fn)
         scale = torch.full((1,), 0.05, device="cuda")
         fn = lambda: ext.fused_add_rms_norm_static_fp8_quant(out, x, r, w, scale, EPS)
+    elif args.profile == "projection":
+        from sm120_rmsnorm import extensions as ext
+        hq, hk = (int(v) for v in args.heads.split(","))
+        n = (hq + 2 * hk) * 128
+        x = torch.randn(t, h, device="cuda", generator=g).to(dt)
+        w = (torch.randn(n, h, device="cuda", generator=g) / h ** 0.5).to(dt)
+        qkv = torch.empty(t, n, device="cuda", dtype=dt)
+        qw = (1 + 0.1 * torch.randn(128, device="cuda", generator=g)).to(dt)
+        inv = 1.0 / (1e6 ** (torch.arange(0, 128, 2, dtype=torch.float32, device="cuda") / 128))
+        f = torch.outer(torch.arange(32768, dtype=torch.float32, device="cuda"), inv)
+        cache = torch.cat((f.cos(), f.sin()), dim=-1)
+        pos = torch.randint(0, 32768, (t,), device="cuda")
+        fn = lambda: ext.qkv_proj_norm_rope_cache_(x, w, qkv, hq, hk, qw, qw, pos, cache)
     elif args.profile == "qkcache":
         from sm120_rmsnorm import extensions as ext
         hq, hk = (int(v) for v in args.heads.split(","))
@@ -1157,7 +1170,7 @@ def main():
     parser.add_argument("--skip-cpu", action="store_true")
     parser.add_argument("--step-only", action="store_true",
                         help="run warm-up and the timed steps only (launch-list captures)")
-    parser.add_argument("--profile", choices=["fused", "rms", "qkkv", "qk", "qkcache", "quant"],
+    parser.add_argument("--profile", choices=["fused", "rms", "qkkv", "qk", "qkcache", "quant", "projection"],
                         help="launch one operator at one shape and exit (ncu driver)")
     parser.add_argument("--tokens", type=int, default=1024)
     parser.add_argument("--hidden", type=int, default=4096)
