@@ -156,7 +156,12 @@ __global__ void __launch_bounds__(256, sizeof(T) == 2 ? 5 : 2) head_cache_kernel
       position = a.positions[token];
       if (kCache != kNoCache && !is_query) {
         slot = a.slots[token];
-        if (slot >= 0 && slot < a.cache_slots) {
+        // Same-type caches read V whatever the slot holds, so that no load
+        // waits on the slot (B = 1024 decode, bf16 cache: 8.24 us against
+        // 8.52); fp8 caches keep the V registers free until the slot is known
+        // (the unconditional form spills there and the 32768-token prefill
+        // loses 1.5%).
+        if (kCache == kSameType || (slot >= 0 && slot < a.cache_slots)) {
           const T* vh = a.value + static_cast<int64_t>(token) * a.value_stride +
                         static_cast<int64_t>(kv_head) * D;
           v_a = load_half<T, kVector>(vh + off_a);
@@ -192,7 +197,8 @@ __global__ void __launch_bounds__(256, sizeof(T) == 2 ? 5 : 2) head_cache_kernel
     }
     store_half<T, kVector>(head + off_a, y_a);
     store_half<T, kVector>(head + off_b, y_b);
-    if (kCache != kNoCache && slot >= 0) {
+    // (query heads keep slot = -1; same-type caches check the range here)
+    if (kCache != kNoCache && slot >= 0 && (kCache != kSameType || slot < a.cache_slots)) {
       const uint32_t block = static_cast<uint32_t>(slot) / a.block_size;
       const uint32_t offset = static_cast<uint32_t>(slot) - block * a.block_size;
       const int64_t base = static_cast<int64_t>(block) * a.block_stride +

@@ -66,8 +66,8 @@ template <typename T>
 struct HeadJob {
   T* head;
   Half8<T> x_lo, x_hi, v_lo, v_hi;
-  int64_t position;
-  int64_t slot;
+  int64_t position;  // as loaded; checked in finish, so that no load waits on it
+  int32_t slot;      // as loaded (KV variant, key heads)
   int kv_head;
   bool is_query;
   bool active;
@@ -122,15 +122,12 @@ __global__ void __launch_bounds__(256, sizeof(T) == 2 ? (kHoistWeights ? 4 : 5) 
       job.position = a.positions[token];
       if constexpr (kStoreKV) {
         if (!job.is_query) {
+          // V is read whatever the slot holds, so that no load waits on the slot
           job.slot = a.slots[token];
-          if (job.slot >= 0 && job.slot < a.cache_slots) {
-            const T* vh =
-                a.value + (static_cast<int64_t>(token) * a.key_heads + job.kv_head) * kHeadDim;
-            job.v_lo = load_half<T, kVector>(vh + lo);
-            job.v_hi = load_half<T, kVector>(vh + hi);
-          } else {
-            job.slot = -1;
-          }
+          const T* vh =
+              a.value + (static_cast<int64_t>(token) * a.key_heads + job.kv_head) * kHeadDim;
+          job.v_lo = load_half<T, kVector>(vh + lo);
+          job.v_hi = load_half<T, kVector>(vh + hi);
         }
       }
     }
@@ -161,8 +158,9 @@ __global__ void __launch_bounds__(256, sizeof(T) == 2 ? (kHoistWeights ? 4 : 5) 
     store_half<T, kVector>(job.head + lo, out_lo);
     store_half<T, kVector>(job.head + hi, out_hi);
     if constexpr (kStoreKV) {
-      if (job.slot >= 0) {
-        const int64_t cache_head = (job.slot * a.key_heads + job.kv_head) * kHeadDim;
+      if (!job.is_query && job.slot >= 0 && job.slot < a.cache_slots) {
+        const int64_t cache_head =
+            (static_cast<int64_t>(job.slot) * a.key_heads + job.kv_head) * kHeadDim;
         store_half<T, kVector>(a.key_cache + cache_head + lo, out_lo);  // same bits as K
         store_half<T, kVector>(a.key_cache + cache_head + hi, out_hi);
         store_half<T, kVector>(a.value_cache + cache_head + lo, job.v_lo);
@@ -192,7 +190,10 @@ int run_heads(HeadArgs<T> a, int threads_per_block, cudaStream_t stream) {
   if (rc != SM120N_OK) return rc;
   // Below about 2048 heads per launch (decode batches up to ~64) the launch is
   // latency-bound and the hoisted-weight form is faster (batch-1 decode:
-  // 2.37 us against 2.48 us); above, occupancy wins.
+  // 2.37 us against 2.48 us); above, occupancy wins. Issuing the next four
+  // heads' loads before finishing the current four (two jobs in flight per
+  // warp) was measured too and lost: 4 blocks/SM make the 32768-token prefill
+  // 267 us against 242 us, 3 blocks/SM 251 us.
   const bool hoist = a.tokens * (a.query_heads + a.key_heads) < 2048;
   auto kernel = vector ? (hoist ? head_norm_rope_kernel<T, kStoreKV, true, true>
                                 : head_norm_rope_kernel<T, kStoreKV, true, false>)
