@@ -10,13 +10,19 @@
 // reference.py:27-49): RMSNorm rounded twice, half-split RoPE, rotated K and
 // V stored at slot_mapping[t] of a [slots, Hk, 128] cache.
 //
-// Tiling: one thread block per 128-token x kTileN-column tile (one or two
-// heads), four warps. The K dimension streams through kStages shared-memory
-// stages of 128-row (A) and kTileN-row (B) x 64-element boxes, loaded by the
-// TMA engine with 128-byte swizzling (thread 0 of warp 0) and consumed by
-// tcgen05.mma.kind::f16 (M 128, N kTileN, K 16; issued by thread 0 of warp 1)
-// into kTileN columns of tensor memory. tcgen05.commit releases each stage
-// back to the loader and finally signals the epilogue.
+// Tiling, one SM per tile: one thread block per 128-token x kTileN-column
+// tile (one or two heads), four warps. The K dimension streams through
+// kStages shared-memory stages of 128-row (A) and kTileN-row (B) x 64-element
+// boxes, loaded by the TMA engine with 128-byte swizzling (thread 0 of warp 0)
+// and consumed by tcgen05.mma.kind::f16 (M 128, N kTileN, K 16; issued by
+// thread 0 of warp 1) into kTileN columns of tensor memory. tcgen05.commit
+// releases each stage back to the loader and finally signals the epilogue.
+//
+// Tiling, two SMs per tile (larger token counts): a cluster of two CTAs per
+// 256-token x 256-column tile, tcgen05.mma.cta_group::2 (M 256, N 256), each
+// CTA staging half of A and half of B in three stages, two pairs resident per
+// two SMs (qkv_gemm_pair_kernel below). The host picks the form per call from
+// a measured wave model.
 //
 // Epilogue: warp w reads TMEM lanes 32w..32w+31, i.e. each thread owns one
 // token row of the tile and, per head, all 128 accumulators of that row. It
@@ -34,6 +40,7 @@
 #include <cudaTypedefs.h>
 
 #include <algorithm>
+#include <map>
 #include <mutex>
 
 #include "head_utils.cuh"
@@ -243,6 +250,47 @@ __device__ __forceinline__ void norm_rope_head(uint32_t* words, const __nv_bfloa
   }
 }
 
+// Epilogue of one 128-token slab of a tile: warp w reads TMEM lanes
+// 32 * (w % 4) onwards (one token row per thread) and the heads hh of the tile
+// with hh % (kWarps / 4) == w / 4; the accumulators of head hh sit in columns
+// [128 hh, 128 hh + 128).
+template <int kHeads, int kWarps>
+__device__ __forceinline__ void store_slab(const GemmArgs& a, uint32_t tmem_base, int warp,
+                                           int lane, int64_t first_row, int first_head) {
+  const int lane_group = warp % 4;
+  const int head_group = warp / 4;
+  const int64_t row = first_row + lane_group * 32 + lane;
+  const bool live = row < a.tokens;
+  int64_t position = -1;
+  int64_t slot = -1;
+  if (live && a.epilogue) {
+    position = a.positions[row];
+    slot = a.slots != nullptr ? a.slots[row] : -1;
+    if (slot >= a.cache_slots) slot = -1;
+  }
+  const bool rope = position >= 0 && position < a.rope_positions;
+#pragma unroll 1
+  for (int hh = head_group; hh < kHeads; hh += kWarps / 4) {
+    uint32_t words[64];
+    load_head(tmem_base + (static_cast<uint32_t>(lane_group * 32) << 16) + hh * kHead, words);
+    if (!live) continue;  // after the warp-wide TMEM load
+    const int head = first_head + hh;
+    __nv_bfloat16* out = a.qkv + row * a.n + static_cast<int64_t>(head) * kHead;
+    if (a.epilogue && rope && head < a.query_heads + a.key_heads) {
+      const bool is_query = head < a.query_heads;
+      norm_rope_head(words, is_query ? a.query_weight : a.key_weight,
+                     a.cos_sin + position * kHead, a.epsilon);
+    }
+    store_head(out, words);
+    if (a.epilogue && rope && slot >= 0 && head >= a.query_heads) {
+      const bool is_key = head < a.query_heads + a.key_heads;
+      const int kv_head = is_key ? head - a.query_heads : head - a.query_heads - a.key_heads;
+      __nv_bfloat16* cache = is_key ? a.key_cache : a.value_cache;
+      store_head(cache + (slot * a.key_heads + kv_head) * kHead, words);
+    }
+  }
+}
+
 template <int kTileN, int kStages, int kWarps>
 __global__ void __launch_bounds__(kWarps * kWarpSize, 1)
     qkv_gemm_kernel(const __grid_constant__ CUtensorMap map_a,
@@ -317,43 +365,11 @@ __global__ void __launch_bounds__(kWarps * kWarpSize, 1)
   }
   __syncwarp();
 
-  // ---- epilogue: every warp; warp w reads TMEM lanes 32 * (w % 4) onwards
-  // and the heads hh with hh % (kWarps / 4) == w / 4 ----
   const bool ready = wait_or_record(&done, 0);
   tc_fence_after();
-  const int lane_group = warp % 4;
-  const int head_group = warp / 4;
-  const int64_t row = static_cast<int64_t>(m_tile) * kTileM + lane_group * 32 + lane;
   if (ready && !aborted) {
-    const bool live = row < a.tokens;
-    int64_t position = -1;
-    int64_t slot = -1;
-    if (live && a.epilogue) {
-      position = a.positions[row];
-      slot = a.slots != nullptr ? a.slots[row] : -1;
-      if (slot >= a.cache_slots) slot = -1;
-    }
-    const bool rope = position >= 0 && position < a.rope_positions;
-#pragma unroll 1
-    for (int hh = head_group; hh < S::kHeads; hh += kWarps / 4) {
-      uint32_t words[64];
-      load_head(tmem_base + (static_cast<uint32_t>(lane_group * 32) << 16) + hh * kHead, words);
-      if (!live) continue;  // after the warp-wide TMEM load
-      const int head = n_tile * S::kHeads + hh;
-      __nv_bfloat16* out = a.qkv + row * a.n + static_cast<int64_t>(head) * kHead;
-      if (a.epilogue && rope && head < a.query_heads + a.key_heads) {
-        const bool is_query = head < a.query_heads;
-        norm_rope_head(words, is_query ? a.query_weight : a.key_weight,
-                       a.cos_sin + position * kHead, a.epsilon);
-      }
-      store_head(out, words);
-      if (a.epilogue && rope && slot >= 0 && head >= a.query_heads) {
-        const bool is_key = head < a.query_heads + a.key_heads;
-        const int kv_head = is_key ? head - a.query_heads : head - a.query_heads - a.key_heads;
-        __nv_bfloat16* cache = is_key ? a.key_cache : a.value_cache;
-        store_head(cache + (slot * a.key_heads + kv_head) * kHead, words);
-      }
-    }
+    store_slab<S::kHeads, kWarps>(a, tmem_base, warp, lane, static_cast<int64_t>(m_tile) * kTileM,
+                                  n_tile * S::kHeads);
   }
   // release tensor memory once every warp is past its loads; after an expired
   // wait, first give in-flight tensor-core work a bounded chance to finish
@@ -366,6 +382,199 @@ __global__ void __launch_bounds__(kWarps * kWarpSize, 1)
     }
     tc_fence_after();
     tmem_dealloc(tmem_base, S::kTmemColumns);
+  }
+}
+
+// ---- 2-SM form: one CTA pair per 256-token x 256-column tile ----------------
+//
+// A cluster of two CTAs on neighbouring SMs computes a 256 x 256 tile with
+// tcgen05.mma.cta_group::2 (M 256, N 256, K 16). CTA r of the pair stages
+// tokens [128 r, 128 r + 128) of the tile (A) and weight rows
+// [128 r, 128 r + 128) of its 256 columns (B); the instruction, issued by
+// CTA 0, reads both CTAs' shared memory and leaves in each CTA's tensor
+// memory its own 128 token rows x all 256 columns. Per 64-element K step an
+// SM therefore loads 32 KiB instead of the 48 KiB of the one-SM 128 x 256
+// tile, for the same tensor-core work.
+//
+// Both CTAs' TMA loads complete on CTA 0's stage barrier (which expects the
+// pair's 64 KiB); CTA 0's commits arrive on the stage-free and done barriers
+// of both CTAs. Each CTA runs the one-SM epilogue on its own 128 rows.
+constexpr int kPairTileM = 2 * kTileM;  // tokens per pair
+constexpr int kPairTileN = 256;         // output columns per pair (two heads)
+constexpr uint32_t kPairStageBytes = 2 * kABytes;  // per CTA: 128 x 64 of A and of B
+
+template <int kStages>
+struct PairShape {
+  static constexpr int kThreads = 4 * kWarpSize;
+  static constexpr int kTmemColumns = kPairTileN;
+  static constexpr size_t kSmem = static_cast<size_t>(kStages) * kPairStageBytes + 1024;
+  static constexpr uint32_t kInstrDesc = (1u << 4) | (1u << 7) | (1u << 10) |
+                                         (static_cast<uint32_t>(kPairTileN >> 3) << 17) |
+                                         (static_cast<uint32_t>(kPairTileM >> 4) << 24);
+};
+
+__device__ __forceinline__ uint32_t cluster_rank() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+  return r;
+}
+
+// All threads of both CTAs of the cluster.
+__device__ __forceinline__ void cluster_sync() {
+  asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::
+                   : "memory");
+}
+
+// Address, in the cluster's shared window, of the variable at `local` in CTA `rank`.
+__device__ __forceinline__ uint32_t peer_shared_address(const void* local, uint32_t rank) {
+  uint32_t r;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(shared_address(local)), "r"(rank));
+  return r;
+}
+
+// TMA tile load into this CTA's shared memory whose completion is counted on
+// `bar`, a barrier of either CTA of the pair (cluster shared address).
+__device__ __forceinline__ void tma_load_2d_pair(void* smem_dst, const CUtensorMap* map, int x, int y,
+                                                 uint32_t bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes"
+      " [%0], [%1, {%2, %3}], [%4];" ::"r"(shared_address(smem_dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(bar)
+      : "memory");
+}
+
+__device__ __forceinline__ void tmem_alloc_pair(uint32_t* slot, uint32_t columns) {
+  asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
+                   shared_address(slot)),
+               "r"(columns)
+               : "memory");
+  asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;" ::: "memory");
+}
+
+__device__ __forceinline__ void tmem_dealloc_pair(uint32_t taddr, uint32_t columns) {
+  asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(columns)
+               : "memory");
+}
+
+__device__ __forceinline__ void mma_bf16_pair(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc,
+                                              uint32_t idesc, uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::2.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(tmem_d),
+      "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+
+// Arrives on the barrier at `bar`'s offset in both CTAs of the pair once all
+// tensor-core work issued so far by this thread has completed.
+__device__ __forceinline__ void mma_commit_pair(uint64_t* bar) {
+  const uint16_t both = 0x3;
+  asm volatile(
+      "tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.multicast::cluster.b64"
+      " [%0], %1;" ::"r"(shared_address(bar)),
+      "h"(both)
+      : "memory");
+}
+
+template <int kStages>
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(4 * kWarpSize, kStages <= 3 ? 2 : 1)
+    qkv_gemm_pair_kernel(const __grid_constant__ CUtensorMap map_a,
+                         const __grid_constant__ CUtensorMap map_b, GemmArgs a) {
+  using S = PairShape<kStages>;
+  extern __shared__ unsigned char dynamic_smem[];
+  __shared__ __align__(8) uint64_t full[kStages];   // used in CTA 0 only
+  __shared__ __align__(8) uint64_t empty[kStages];
+  __shared__ __align__(8) uint64_t done;
+  __shared__ uint32_t tmem_slot;
+  __shared__ int aborted;
+  unsigned char* tiles = reinterpret_cast<unsigned char*>(
+      (reinterpret_cast<uintptr_t>(dynamic_smem) + 1023) & ~uintptr_t{1023});
+  const int warp = threadIdx.x / kWarpSize;
+  const int lane = threadIdx.x & (kWarpSize - 1);
+  const uint32_t rank = cluster_rank();
+  const int n_tile = blockIdx.x / 2;
+  const int m_pair = blockIdx.y;
+  const int64_t first_row = static_cast<int64_t>(m_pair) * kPairTileM + rank * kTileM;
+  // A CTA whose rows all lie past the end loads the last token rows instead
+  // (its results are never stored), so that no box starts out of range.
+  const int a_row = static_cast<int>(std::min<int64_t>(first_row, a.tokens - 1));
+  const int b_row = n_tile * kPairTileN + static_cast<int>(rank) * kTileM;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < kStages; ++s) {
+      mbarrier_init(&full[s], 1);
+      mbarrier_init(&empty[s], 1);
+    }
+    mbarrier_init(&done, 1);
+    aborted = 0;
+    fence_mbarrier_init();
+  }
+  if (warp == 0) tmem_alloc_pair(&tmem_slot, S::kTmemColumns);
+  tc_fence_before();
+  cluster_sync();  // barriers of both CTAs initialised, the pair's TMEM allocated
+  tc_fence_after();
+  const uint32_t tmem_base = tmem_slot;
+  wait_for_upstream_grid();
+  release_downstream_grid();
+
+  if (warp == 0 && lane == 0) {
+    // loader (both CTAs): this CTA's halves of A and B, counted on CTA 0's barrier
+    for (int k = 0; k < a.k_tiles; ++k) {
+      const int s = k % kStages;
+      if (k >= kStages && !wait_or_record(&empty[s], ((k / kStages) - 1) & 1)) {
+        atomicExch(&aborted, 1);
+        break;
+      }
+      if (atomicAdd(&aborted, 0)) break;
+      unsigned char* stage = tiles + static_cast<size_t>(s) * kPairStageBytes;
+      if (rank == 0) mbarrier_arrive_expect_tx(&full[s], 2 * kPairStageBytes);
+      const uint32_t bar = peer_shared_address(&full[s], 0);
+      tma_load_2d_pair(stage, &map_a, k * kTileK, a_row, bar);
+      tma_load_2d_pair(stage + kABytes, &map_b, k * kTileK, b_row, bar);
+    }
+  } else if (warp == 1 && lane == 0 && rank == 0) {
+    // tensor-core issuer (CTA 0)
+    for (int k = 0; k < a.k_tiles; ++k) {
+      const int s = k % kStages;
+      if (!wait_or_record(&full[s], (k / kStages) & 1)) {
+        atomicExch(&aborted, 1);
+        break;
+      }
+      tc_fence_after();
+      const unsigned char* stage = tiles + static_cast<size_t>(s) * kPairStageBytes;
+      const uint64_t adesc = smem_descriptor(stage);
+      const uint64_t bdesc = smem_descriptor(stage + kABytes);
+#pragma unroll
+      for (int kk = 0; kk < kTileK / kMmaK; ++kk) {
+        mma_bf16_pair(tmem_base, adesc + 2 * kk, bdesc + 2 * kk, S::kInstrDesc, (k | kk) != 0);
+      }
+      mma_commit_pair(&empty[s]);
+    }
+    mma_commit_pair(&done);  // both CTAs, once every MMA issued above has completed
+  }
+  __syncwarp();
+
+  const bool ready = wait_or_record(&done, 0);
+  tc_fence_after();
+  if (ready && !aborted) {
+    store_slab<kPairTileN / kHead, 4>(a, tmem_base, warp, lane, first_row,
+                                      n_tile * (kPairTileN / kHead));
+  }
+  // Both CTAs past their TMEM loads (and, after an expired wait, a bounded
+  // chance for the pair's tensor-core work to finish) before the pair's
+  // tensor memory is released; no CTA leaves while the other may still
+  // signal its barriers or read its shared memory.
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 0 && !ready) {
+    if (lane == 0) mbarrier_wait_bounded(&done, 0);
+    __syncwarp();
+  }
+  cluster_sync();
+  if (warp == 0) {
+    tc_fence_after();
+    tmem_dealloc_pair(tmem_base, S::kTmemColumns);
   }
 }
 
@@ -420,6 +629,72 @@ int launch_gemm(const CUtensorMap& map_a, const void* qkv_weight, int64_t n, int
   const dim3 grid(static_cast<unsigned>(n / kTileN),
                   static_cast<unsigned>((tokens + kTileM - 1) / kTileM));
   return launch(kernel, grid, dim3(S::kThreads), S::kSmem, stream, map_a, map_b, a);
+}
+
+template <int kStages>
+int launch_gemm_pair(const CUtensorMap& map_a, const void* qkv_weight, int64_t n,
+                     int64_t hidden_size, const GemmArgs& a, int64_t tokens, cudaStream_t stream) {
+  using S = PairShape<kStages>;
+  CUtensorMap map_b;
+  int rc = make_map(&map_b, qkv_weight, n, hidden_size, kTileM);
+  if (rc != SM120N_OK) return rc;
+  auto kernel = qkv_gemm_pair_kernel<kStages>;
+  rc = allow_dynamic_smem(reinterpret_cast<const void*>(kernel), S::kSmem);
+  if (rc != SM120N_OK) return rc;
+  const dim3 grid(static_cast<unsigned>(2 * (n / kPairTileN)),
+                  static_cast<unsigned>((tokens + kPairTileM - 1) / kPairTileM));
+  return launch(kernel, grid, dim3(S::kThreads), S::kSmem, stream, map_a, map_b, a);
+}
+
+// CTA pairs of qkv_gemm_pair_kernel<kStages> resident at once on `device`
+// (the current device), cached per device: SMs x blocks per SM / 2, blocks
+// per SM limited by shared memory, registers and tensor memory (512
+// columns). Computed from the kernel's resources because the runtime's
+// cluster occupancy query reports one pair per two SMs for this kernel,
+// while ncu's launch statistics show two blocks per SM (register and shared
+// memory limits 2, 7.8 of 8 warps active).
+template <int kStages>
+int resident_pairs(int device, int* out) {
+  static std::mutex mutex;
+  static std::map<int, int> cache;
+  {
+    std::lock_guard<std::mutex> lock(mutex);
+    auto it = cache.find(device);
+    if (it != cache.end()) {
+      *out = it->second;
+      return SM120N_OK;
+    }
+  }
+  using S = PairShape<kStages>;
+  cudaFuncAttributes attributes;
+  cudaError_t err = cudaFuncGetAttributes(&attributes, qkv_gemm_pair_kernel<kStages>);
+  int sms = 0, smem_per_sm = 0, reserved = 0, regs_per_sm = 0;
+  if (err == cudaSuccess) err = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, device);
+  if (err == cudaSuccess) {
+    err = cudaDeviceGetAttribute(&smem_per_sm, cudaDevAttrMaxSharedMemoryPerMultiprocessor, device);
+  }
+  if (err == cudaSuccess) {
+    err = cudaDeviceGetAttribute(&reserved, cudaDevAttrReservedSharedMemoryPerBlock, device);
+  }
+  if (err == cudaSuccess) {
+    err = cudaDeviceGetAttribute(&regs_per_sm, cudaDevAttrMaxRegistersPerMultiprocessor, device);
+  }
+  if (err != cudaSuccess) {
+    return fail(SM120N_ERR_CUDA, "querying the projection kernel's resources failed: %s",
+                cudaGetErrorString(err));
+  }
+  const int64_t smem_per_block =
+      static_cast<int64_t>(S::kSmem) + static_cast<int64_t>(attributes.sharedSizeBytes) + reserved;
+  const int64_t regs_per_block = static_cast<int64_t>((attributes.numRegs + 7) / 8 * 8) * S::kThreads;
+  const int64_t per_sm = std::max<int64_t>(
+      1, std::min({static_cast<int64_t>(smem_per_sm) / smem_per_block,
+                   static_cast<int64_t>(regs_per_sm) / regs_per_block,
+                   static_cast<int64_t>(512 / S::kTmemColumns)}));
+  const int pairs = static_cast<int>(std::max<int64_t>(1, sms * per_sm / 2));
+  std::lock_guard<std::mutex> lock(mutex);
+  cache[device] = pairs;
+  *out = pairs;
+  return SM120N_OK;
 }
 
 }  // namespace
@@ -508,11 +783,37 @@ extern "C" int sm120n_qkv_proj_norm_rope_cache(
              epsilon,
              epilogue};
   const cudaStream_t st = static_cast<cudaStream_t>(stream);
-  // Measured on B200 (Qwen3-8B-shaped projection, N = 6144, K = 4096): one
-  // head per block and six stages for up to 256 tokens (33 us at 1 token,
-  // against 37 us with two heads per block), two heads per block and four
-  // stages above (1360 us at 32768 tokens, against 2296 us with one head);
-  // two blocks per SM or eight warps per block were slower everywhere.
-  if (tokens <= 256) return launch_gemm<128, 6, 4>(map_a, qkv_weight, n, hidden_size, a, tokens, st);
-  return launch_gemm<256, 4, 4>(map_a, qkv_weight, n, hidden_size, a, tokens, st);
+  // The launch form comes from a wave model measured on B200 (Qwen3-8B-shaped
+  // projection, N = 6144, K = 4096, graphs of back-to-back calls): with
+  // tiles resident at once on the device, a launch takes
+  // ceil(tiles / resident) waves, and one 64-element K step of a wave costs
+  // about 0.47 us for 128 x 128 tiles (one block per SM, six stages), 0.57 us
+  // for 128 x 256 tiles (one block per SM, four stages) and 0.80 us for
+  // 256 x 256 tiles on CTA pairs (two pairs per two SMs, three stages). The
+  // cheapest estimate wins: 1-384 tokens one-head tiles (1 token 33 us),
+  // 512-768 two-head tiles (512: 42 us against 61 / 47), from 1024 the pairs
+  // (1024: 59 us against 88 / 72; 4096: 163 us against 301 / 197). A pair
+  // per 256 x 256 tile with six stages and one pair per two SMs measured
+  // 192 us at 4096 tokens: the second resident pair, which overlaps one
+  // tile's epilogue with another's main loop, is what the three stages buy.
+  DeviceInfo dev;
+  rc = current_device_info(&dev);
+  if (rc != SM120N_OK) return rc;
+  int pairs = 1;
+  rc = resident_pairs<3>(dev.device, &pairs);
+  if (rc != SM120N_OK) return rc;
+  const int64_t sms = dev.sm_count;
+  const int64_t m128 = (tokens + kTileM - 1) / kTileM;
+  const int64_t m256 = (tokens + kPairTileM - 1) / kPairTileM;
+  auto waves = [](int64_t tiles, int64_t slots) { return (tiles + slots - 1) / std::max<int64_t>(slots, 1); };
+  const int64_t cost_one_head = waves(m128 * (n / 128), sms) * 47;
+  const int64_t cost_two_heads = waves(m128 * (n / 256), sms) * 57;
+  const int64_t cost_pair = waves(m256 * (n / kPairTileN), pairs) * 80;
+  if (cost_one_head <= cost_two_heads && cost_one_head <= cost_pair) {
+    return launch_gemm<128, 6, 4>(map_a, qkv_weight, n, hidden_size, a, tokens, st);
+  }
+  if (cost_two_heads <= cost_pair) {
+    return launch_gemm<256, 4, 4>(map_a, qkv_weight, n, hidden_size, a, tokens, st);
+  }
+  return launch_gemm_pair<3>(map_a, qkv_weight, n, hidden_size, a, tokens, st);
 }
