@@ -36,6 +36,7 @@
 // counter (read with sm120n_get_device_faults), the block skips the rest of
 // its work (waiting, again bounded, for its own asynchronous operations) and
 // releases its tensor memory.
+#include <cooperative_groups.h>
 #include <cuda.h>
 #include <cudaTypedefs.h>
 
@@ -578,6 +579,240 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(4 * kWarpSize, kStag
   }
 }
 
+// ---- weight streaming for a few tokens -------------------------------------
+//
+// With at most kGemvMaxTokens tokens the projection only has to stream the
+// weight matrix once (2 N K bytes), which the tensor-core tiles do at far
+// below the HBM rate. Here a cluster of kGemvSplits CTAs owns one head (128
+// weight rows) and CTA s reduces K slice s of all 128 rows for every token.
+// Lane j = lane % 8 of lane group g = lane / 8 in warp w owns rows
+// 16w + 4i + g (i = 0..3) and, in each of them, the 16-byte chunks at
+// k = 64m + 8j of the slice (eight lanes cover 128 contiguous bytes). The
+// chunks stream through a ring of kGemvRing phases in shared memory by
+// cp.async (no registers held while in flight): phase m brings chunk m of
+// each of the lane's four rows, the next phases are in flight while one is
+// used. Each chunk is multiplied with the tokens' activations (bf16 in
+// shared memory, read once per chunk for all four rows) in a fused
+// multiply-add chain in element order, chunks in K order, and the eight
+// lanes of a row combine by the butterfly 4, 2, 1. The slices' partial sums
+// stay in each CTA's shared memory; after a cluster barrier CTA s sums, for
+// its tokens (t % kGemvSplits == s), the partials of CTAs 0, 1, ... in that
+// order through distributed shared memory, rounds to bf16 and runs the Q/K
+// epilogue with eight lanes per head row exactly as head_norm_rope_kernel
+// does. Every summation order is fixed, so the fused and the plain result of
+// this path agree bit for bit with its own output followed by the Q/K kernel.
+constexpr int kGemvSplits = 8;
+constexpr int kGemvThreads = 256;  // 8 warps x 16 rows = one head
+constexpr int kGemvMaxTokens = 4;
+constexpr int kGemvMaxSlice = 1024;  // K / kGemvSplits, a multiple of 64
+constexpr int kGemvRing = 4;         // phases in flight
+// one phase: one 16-byte chunk of each of the thread's 4 rows
+constexpr uint32_t kGemvPhaseBytes = 4 * 16 * kGemvThreads;
+
+__device__ __forceinline__ void cp_async16(void* smem_dst, const void* gmem_src) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(shared_address(smem_dst)),
+               "l"(gmem_src)
+               : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() {
+  asm volatile("cp.async.commit_group;" ::: "memory");
+}
+template <int kPending>
+__device__ __forceinline__ void cp_async_wait() {
+  asm volatile("cp.async.wait_group %0;" ::"n"(kPending) : "memory");
+}
+
+template <int kTokens>
+__global__ void __launch_bounds__(kGemvThreads, 3) qkv_gemv_kernel(const __nv_bfloat16* hidden,
+                                                                  const __nv_bfloat16* weight,
+                                                                  GemmArgs a, int hidden_size) {
+  namespace cg = cooperative_groups;
+  // dynamic: kGemvRing phases of kGemvPhaseBytes, then [kTokens][slice] bf16
+  extern __shared__ uint4 gemv_dynamic[];
+  __shared__ float partial[kTokens][kHead];
+  __shared__ __align__(16) __nv_bfloat16 rows[kTokens][kHead];
+  cg::cluster_group cluster = cg::this_cluster();
+  const int split = static_cast<int>(cluster.block_rank());
+  const int splits = static_cast<int>(cluster.num_blocks());
+  const int head = blockIdx.y;
+  const int warp = threadIdx.x / kWarpSize;
+  const int lane = threadIdx.x & (kWarpSize - 1);
+  const int g = lane >> 3;
+  const int j = lane & 7;
+  const int tokens = static_cast<int>(a.tokens);
+  const int slice = hidden_size / splits;
+  const int chunks = slice / 64;  // per lane and row
+  const int64_t k0 = static_cast<int64_t>(split) * slice;
+  unsigned char* ring = reinterpret_cast<unsigned char*>(gemv_dynamic);
+  __nv_bfloat16* xs = reinterpret_cast<__nv_bfloat16*>(ring + kGemvRing * kGemvPhaseBytes);
+
+  // Ask for this CTA's 128 weight-row slices in L2 at once (a prefetch
+  // returns no data, so it may precede the wait for the upstream grid: L2
+  // stays coherent with any write that grid makes).
+  if (threadIdx.x < kHead) {
+    const __nv_bfloat16* w_slice =
+        weight + (static_cast<int64_t>(head) * kHead + threadIdx.x) * hidden_size + k0;
+    asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(w_slice),
+                 "r"(static_cast<uint32_t>(slice * sizeof(__nv_bfloat16)))
+                 : "memory");
+  }
+  wait_for_upstream_grid();
+  release_downstream_grid();
+
+  // The epilogue's lanes (eight per head row this CTA finishes: tokens
+  // t = split, split + splits, ...) fetch their token's position and slot
+  // now and the cos/sin row and norm weights right after the main loop, so
+  // that none of these loads is on the path after the cluster barrier.
+  const int mine = tokens > split ? (tokens - split + splits - 1) / splits : 0;
+  const bool epilogue_warp = warp * kWarpSize < mine * 8;
+  const int er = threadIdx.x / 8;  // head row of an epilogue lane
+  const bool live = epilogue_warp && er < mine;
+  const int et = split + er * splits;
+  int64_t position = -1;
+  int64_t slot = -1;
+  if (live && a.epilogue) {
+    position = a.positions[et];
+    slot = a.slots != nullptr ? a.slots[et] : -1;
+  }
+
+  // this thread's rows: 16 warp + 4 i + g; its chunk m of row i sits at
+  // ring + (m % kGemvRing) * kGemvPhaseBytes + (i * kGemvThreads + threadIdx.x) * 16.
+  // Every phase commits a group (an empty one past the last chunk), so
+  // waiting for all but kGemvRing - 1 groups always means phase m has landed.
+  const __nv_bfloat16* w_lane =
+      weight + (static_cast<int64_t>(head) * kHead + 16 * warp + g) * hidden_size + k0 + 8 * j;
+  auto issue = [&](int m) {
+    if (m < chunks) {
+      unsigned char* stage = ring + (m % kGemvRing) * kGemvPhaseBytes;
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        cp_async16(stage + (i * kGemvThreads + threadIdx.x) * 16,
+                   w_lane + static_cast<int64_t>(4 * i) * hidden_size + 64 * m);
+      }
+    }
+    cp_async_commit();
+  };
+#pragma unroll
+  for (int m = 0; m < kGemvRing; ++m) issue(m);
+
+  // this slice of every token's activations (zero past the last token)
+  for (int i = threadIdx.x; i < kTokens * (slice / 8); i += kGemvThreads) {
+    const int t = i / (slice / 8);
+    const int c = (i - t * (slice / 8)) * 8;
+    uint4 v = make_uint4(0, 0, 0, 0);
+    if (t < tokens) v = load16(hidden + static_cast<int64_t>(t) * hidden_size + k0 + c);
+    *reinterpret_cast<uint4*>(xs + t * slice + c) = v;
+  }
+  __syncthreads();
+
+  float acc[4][kTokens];
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+#pragma unroll
+    for (int t = 0; t < kTokens; ++t) acc[i][t] = 0.0f;
+  }
+#pragma unroll 1
+  for (int m = 0; m < chunks; ++m) {
+    cp_async_wait<kGemvRing - 1>();
+    const unsigned char* stage = ring + (m % kGemvRing) * kGemvPhaseBytes;
+    float2 wf[4][4];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const uint4 raw = *reinterpret_cast<const uint4*>(stage + (i * kGemvThreads + threadIdx.x) * 16);
+      Half8<__nv_bfloat16> h;
+      h.w[0] = raw.x; h.w[1] = raw.y; h.w[2] = raw.z; h.w[3] = raw.w;
+      unpack_pairs<__nv_bfloat16>(h, wf[i]);
+    }
+#pragma unroll
+    for (int t = 0; t < kTokens; ++t) {
+      const uint4 raw = *reinterpret_cast<const uint4*>(xs + t * slice + 64 * m + 8 * j);
+      Half8<__nv_bfloat16> h;
+      h.w[0] = raw.x; h.w[1] = raw.y; h.w[2] = raw.z; h.w[3] = raw.w;
+      float2 xf[4];
+      unpack_pairs<__nv_bfloat16>(h, xf);
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        float v = acc[i][t];
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          v = __fmaf_rn(wf[i][e].x, xf[e].x, v);
+          v = __fmaf_rn(wf[i][e].y, xf[e].y, v);
+        }
+        acc[i][t] = v;
+      }
+    }
+    // this thread alone reads and refills its slots of the stage
+    issue(m + kGemvRing);
+  }
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+#pragma unroll
+    for (int t = 0; t < kTokens; ++t) {
+      const float total = group_allreduce_sum<8>(acc[i][t]);
+      if (j == 0) partial[t][16 * warp + 4 * i + g] = total;
+    }
+  }
+  if (slot >= a.cache_slots) slot = -1;
+  const bool rope = position >= 0 && position < a.rope_positions;
+  const bool norm = live && a.epilogue && rope && head < a.query_heads + a.key_heads;
+  const int lo = 8 * j;
+  const int hi = kHead / 2 + lo;
+  float2 c[4], sn[4];
+  Half8<__nv_bfloat16> nw_lo{}, nw_hi{};
+  if (norm) {
+    const __nv_bfloat16* nw = head < a.query_heads ? a.query_weight : a.key_weight;
+    nw_lo = load_half<__nv_bfloat16, true>(nw + lo);
+    nw_hi = load_half<__nv_bfloat16, true>(nw + hi);
+    load8_pairs<true>(a.cos_sin + position * kHead + lo, c);
+    load8_pairs<true>(a.cos_sin + position * kHead + hi, sn);
+  }
+  cluster.sync();  // every CTA's partial sums are in place
+
+  // sum the splits' partials of each token this CTA finishes, in rank order
+  for (int idx = threadIdx.x; idx < mine * kHead; idx += kGemvThreads) {
+    const int r = idx / kHead;
+    const int col = idx - r * kHead;
+    const int t = split + r * splits;
+    float sum = *cluster.map_shared_rank(&partial[t][col], 0);
+    for (int s = 1; s < splits; ++s) sum = __fadd_rn(sum, *cluster.map_shared_rank(&partial[t][col], s));
+    rows[r][col] = __float2bfloat16_rn(sum);
+  }
+  __syncthreads();
+
+  // Q/K epilogue, eight lanes per head row (head_norm_rope_kernel's lane map)
+  if (epilogue_warp) {
+    Half8<__nv_bfloat16> x_lo{}, x_hi{};
+    if (live) {
+      x_lo = load_half<__nv_bfloat16, true>(&rows[er][lo]);
+      x_hi = load_half<__nv_bfloat16, true>(&rows[er][hi]);
+    }
+    const float2 sq = half_sum_squares<__nv_bfloat16>(
+        x_hi, half_sum_squares<__nv_bfloat16>(x_lo, make_float2(0.f, 0.f)));
+    const float total = group_allreduce_sum<8>(__fadd_rn(sq.x, sq.y));  // all lanes
+    Half8<__nv_bfloat16> y_lo = x_lo, y_hi = x_hi;
+    if (norm) {
+      const float inv = head_inverse_rms<kHead>(make_float2(total, 0.0f), a.epsilon);
+      const Half8<__nv_bfloat16> n_lo = normalise_half<__nv_bfloat16>(x_lo, nw_lo, inv);
+      const Half8<__nv_bfloat16> n_hi = normalise_half<__nv_bfloat16>(x_hi, nw_hi, inv);
+      rotate_half<__nv_bfloat16>(n_lo, n_hi, c, sn, y_lo, y_hi);
+    }
+    if (live) {
+      __nv_bfloat16* out = a.qkv + static_cast<int64_t>(et) * a.n + static_cast<int64_t>(head) * kHead;
+      store_half<__nv_bfloat16, true>(out + lo, y_lo);
+      store_half<__nv_bfloat16, true>(out + hi, y_hi);
+      if (a.epilogue && rope && slot >= 0 && head >= a.query_heads) {
+        const bool is_key = head < a.query_heads + a.key_heads;
+        const int kv_head = is_key ? head - a.query_heads : head - a.query_heads - a.key_heads;
+        __nv_bfloat16* cache =
+            (is_key ? a.key_cache : a.value_cache) + (slot * a.key_heads + kv_head) * kHead;
+        store_half<__nv_bfloat16, true>(cache + lo, y_lo);
+        store_half<__nv_bfloat16, true>(cache + hi, y_hi);
+      }
+    }
+  }
+  cluster.sync();  // no CTA leaves while another may still read its partial sums
+}
+
 // ---- host ----------------------------------------------------------------
 PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder(int* rc) {
   static std::once_flag once;
@@ -644,6 +879,41 @@ int launch_gemm_pair(const CUtensorMap& map_a, const void* qkv_weight, int64_t n
   const dim3 grid(static_cast<unsigned>(2 * (n / kPairTileN)),
                   static_cast<unsigned>((tokens + kPairTileM - 1) / kPairTileM));
   return launch(kernel, grid, dim3(S::kThreads), S::kSmem, stream, map_a, map_b, a);
+}
+
+template <int kTokens>
+int launch_gemv(const void* hidden, const void* qkv_weight, const GemmArgs& a, int64_t n,
+                int64_t hidden_size, cudaStream_t stream) {
+  auto kernel = qkv_gemv_kernel<kTokens>;
+  const size_t smem = kGemvRing * kGemvPhaseBytes +
+                      static_cast<size_t>(kTokens) * (hidden_size / kGemvSplits) * sizeof(__nv_bfloat16);
+  int rc = allow_dynamic_smem(reinterpret_cast<const void*>(kernel), smem);
+  if (rc != SM120N_OK) return rc;
+  cudaLaunchConfig_t config = {};
+  config.gridDim = dim3(kGemvSplits, static_cast<unsigned>(n / kHead));
+  config.blockDim = dim3(kGemvThreads);
+  config.dynamicSmemBytes = smem;
+  config.stream = stream;
+  cudaLaunchAttribute attribute[2];
+  attribute[0].id = cudaLaunchAttributeClusterDimension;
+  attribute[0].val.clusterDim.x = kGemvSplits;
+  attribute[0].val.clusterDim.y = 1;
+  attribute[0].val.clusterDim.z = 1;
+  config.attrs = attribute;
+  config.numAttrs = 1;
+  if (programmatic_launch_enabled()) {
+    attribute[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attribute[1].val.programmaticStreamSerializationAllowed = 1;
+    config.numAttrs = 2;
+  }
+  const cudaError_t err =
+      cudaLaunchKernelEx(&config, kernel, static_cast<const __nv_bfloat16*>(hidden),
+                         static_cast<const __nv_bfloat16*>(qkv_weight), a,
+                         static_cast<int>(hidden_size));
+  if (err != cudaSuccess) {
+    return fail(SM120N_ERR_CUDA, "kernel launch failed: %s", cudaGetErrorString(err));
+  }
+  return SM120N_OK;
 }
 
 // CTA pairs of qkv_gemm_pair_kernel<kStages> resident at once on `device`
@@ -762,9 +1032,6 @@ extern "C" int sm120n_qkv_proj_norm_rope_cache(
     return fail(SM120N_ERR_UNSUPPORTED, "the fused projection needs 16-byte-aligned buffers");
   }
   const int64_t n = heads * kHead;
-  CUtensorMap map_a;
-  int rc = make_map(&map_a, hidden, tokens, hidden_size, kTileM);
-  if (rc != SM120N_OK) return rc;
   GemmArgs a{static_cast<__nv_bfloat16*>(qkv),
              static_cast<const __nv_bfloat16*>(query_weight),
              static_cast<const __nv_bfloat16*>(key_weight),
@@ -783,6 +1050,18 @@ extern "C" int sm120n_qkv_proj_norm_rope_cache(
              epsilon,
              epilogue};
   const cudaStream_t st = static_cast<cudaStream_t>(stream);
+  // Up to four tokens stream the weights on the CUDA cores (2 N K bytes,
+  // HBM-bound); hidden a multiple of 512 up to 8192 (eight slices of whole
+  // 64-element chunks).
+  if (tokens <= kGemvMaxTokens && hidden_size % (64 * kGemvSplits) == 0 &&
+      hidden_size / kGemvSplits <= kGemvMaxSlice) {
+    if (tokens == 1) return launch_gemv<1>(hidden, qkv_weight, a, n, hidden_size, st);
+    if (tokens == 2) return launch_gemv<2>(hidden, qkv_weight, a, n, hidden_size, st);
+    return launch_gemv<4>(hidden, qkv_weight, a, n, hidden_size, st);
+  }
+  CUtensorMap map_a;
+  int rc = make_map(&map_a, hidden, tokens, hidden_size, kTileM);
+  if (rc != SM120N_OK) return rc;
   // The launch form comes from a wave model measured on B200 (Qwen3-8B-shaped
   // projection, N = 6144, K = 4096, graphs of back-to-back calls): with
   // tiles resident at once on the device, a launch takes

@@ -43,13 +43,15 @@ def rope_table(positions=4096):
     return torch.cat((f.cos(), f.sin()), dim=-1)
 
 
-# Launch forms (wave model in csrc/qkv_gemm.cu): one-head tiles for up to a
-# wave of 128 x 128 tiles, two-head tiles next, CTA-pair 256 x 256 tiles for
-# the largest calls. The 1300- and 2048-token cases with 48 heads run on CTA
-# pairs; at 1300 tokens the second CTA of the last pair has no token rows.
+# Launch forms (csrc/qkv_gemm.cu): up to eight tokens with hidden a multiple
+# of 512 stream the weights on the CUDA cores (1, 5 and 8 tokens here);
+# otherwise the wave model picks one-head tiles for up to a wave of 128 x 128
+# tiles, two-head tiles next, CTA-pair 256 x 256 tiles for the largest calls.
+# The 1300- and 2048-token cases with 48 heads run on CTA pairs; at 1300
+# tokens the second CTA of the last pair has no token rows.
 @pytest.mark.parametrize("tokens, hidden, hq, hk", [
     (1, 64, 2, 0), (128, 256, 2, 1), (300, 1024, 4, 2), (257, 4096, 32, 8), (1000, 2048, 16, 8),
-    (1300, 512, 32, 8), (2048, 1024, 32, 8)])
+    (1300, 512, 32, 8), (2048, 1024, 32, 8), (1, 512, 2, 1), (5, 1024, 4, 2), (8, 4096, 32, 8)])
 def test_plain_gemm_is_exact_on_exact_inputs(tokens, hidden, hq, hk):
     a, w = operands(tokens, hidden, hq, hk, tokens, exact=True)
     out = torch.zeros(tokens, w.shape[0], device=DEV, dtype=torch.bfloat16)
@@ -57,8 +59,8 @@ def test_plain_gemm_is_exact_on_exact_inputs(tokens, hidden, hq, hk):
     assert_bitwise_equal(out, a @ w.t(), what="GEMM")
 
 
-@pytest.mark.parametrize("tokens, hidden", [(1, 4096), (2, 4096), (64, 4096), (513, 1024),
-                                           (1300, 1024), (2048, 4096)])
+@pytest.mark.parametrize("tokens, hidden", [(1, 4096), (2, 4096), (7, 2048), (64, 4096),
+                                           (513, 1024), (1300, 1024), (2048, 4096)])
 def test_plain_gemm_random_inputs_within_one_ulp(tokens, hidden):
     a, w = operands(tokens, hidden, 32, 8, 5, exact=False)
     out = torch.empty(tokens, w.shape[0], device=DEV, dtype=torch.bfloat16)
@@ -75,7 +77,7 @@ def test_plain_gemm_random_inputs_within_one_ulp(tokens, hidden):
 
 @pytest.mark.parametrize("tokens, hidden, hq, hk", [
     (1, 256, 16, 8), (37, 1024, 8, 4), (128, 4096, 32, 8), (700, 2048, 16, 8),
-    (1300, 512, 32, 8), (2048, 1024, 32, 8)])
+    (1300, 512, 32, 8), (2048, 1024, 32, 8), (1, 4096, 32, 8), (3, 1024, 8, 4), (8, 512, 16, 8)])
 @pytest.mark.parametrize("with_cache", [True, False])
 def test_fused_epilogue_equals_gemm_then_qk_kernel(tokens, hidden, hq, hk, with_cache):
     a, w = operands(tokens, hidden, hq, hk, 7 + tokens, exact=False)
@@ -84,7 +86,8 @@ def test_fused_epilogue_equals_gemm_then_qk_kernel(tokens, hidden, hq, hk, with_
     kw = (1 + 0.1 * torch.randn(128, device=DEV, generator=g)).bfloat16()
     table = rope_table()
     pos = torch.randint(0, 4096, (tokens,), device=DEV, generator=g)
-    pos[0] = -1                  # out of range: the token stays the plain GEMM output
+    if tokens > 1:
+        pos[0] = -1              # out of range: the token stays the plain GEMM output
     if tokens > 2:
         pos[1] = 4096
     slots_total = (tokens + 16) * 2
