@@ -585,6 +585,16 @@ def vllm_ops():
         return None
 
 
+def flashinfer_fused_add_rmsnorm():
+    """FlashInfer's in-place residual add + RMSNorm (an installed library
+    kernel, timed as a comparator only), or None when it does not load."""
+    try:
+        from flashinfer import norm
+        return norm.fused_add_rmsnorm
+    except Exception:  # noqa: BLE001 - optional comparator
+        return None
+
+
 def extension_suite(flush: Flusher, dist: Dist, args) -> dict:
     """The engine-side extensions (sm120_rmsnorm.extensions) at decode and
     prefill shapes, each beside the unfused vLLM pair that does the same work
@@ -760,23 +770,30 @@ def extension_suite(flush: Flusher, dist: Dist, args) -> dict:
     fp4_case("fused add + rms_norm_nvfp4_quant bf16 1024x4096", 1024, 4096)
     fp4_case("fused add + rms_norm_nvfp4_quant prefill bf16 65536x8192", 65536, 8192)
 
-    # the headline op beside vLLM's residual add + RMSNorm on the same shapes
-    if vllm is not None:
-        import sm120_rmsnorm as ops
-        C, _ = vllm
-        for t, h in ((1024, 4096), (65536, 8192)):
-            nbytes = fused_bytes(t, h, 2)
-            w = (1 + 0.1 * torch.randn(h, device="cuda", generator=g)).to(bf)
-            sets = [(torch.randn(t, h, device="cuda", generator=g).to(bf),
-                     torch.randn(t, h, device="cuda", generator=g).to(bf))
-                    for _ in range(sets_for(nbytes))]
-            record(f"fused_add_rms_norm_inplace bf16 {t}x{h}",
-                   [lambda x=x, r=r: ops.fused_add_rms_norm_inplace(x, r, w, EPS) for x, r in sets],
-                   nbytes)
+    # the headline op beside vLLM's and FlashInfer's residual add + RMSNorm on
+    # the same shapes (library comparators: timed here, never on the product path)
+    import sm120_rmsnorm as ops
+    flashinfer_norm = flashinfer_fused_add_rmsnorm()
+    for t, h in ((1024, 4096), (65536, 8192)):
+        nbytes = fused_bytes(t, h, 2)
+        w = (1 + 0.1 * torch.randn(h, device="cuda", generator=g)).to(bf)
+        sets = [(torch.randn(t, h, device="cuda", generator=g).to(bf),
+                 torch.randn(t, h, device="cuda", generator=g).to(bf))
+                for _ in range(sets_for(nbytes))]
+        record(f"fused_add_rms_norm_inplace bf16 {t}x{h}",
+               [lambda x=x, r=r: ops.fused_add_rms_norm_inplace(x, r, w, EPS) for x, r in sets],
+               nbytes)
+        if vllm is not None:
+            C, _ = vllm
             record(f"fused_add_rms_norm_inplace bf16 {t}x{h} [vLLM fused_add_rms_norm]",
                    [lambda x=x, r=r: C.fused_add_rms_norm(x, r, w, EPS) for x, r in sets],
                    nbytes, comparator=True)
-            del sets
+        if flashinfer_norm is not None:
+            record(f"fused_add_rms_norm_inplace bf16 {t}x{h} [FlashInfer fused_add_rmsnorm]",
+                   [lambda x=x, r=r: flashinfer_norm(x, r, w, EPS) for x, r in sets],
+                   nbytes, comparator=True)
+        del sets
+    out["flashinfer_comparator"] = "loaded" if flashinfer_norm is not None else "unavailable"
     out["vllm_comparator"] = "loaded" if vllm is not None else "unavailable"
     return out
 

@@ -187,7 +187,11 @@ __global__ void __launch_bounds__(kMaxThreads, kMinBlocks) norm_fp4_cta_kernel(F
 #pragma unroll
     for (int i = 0; i < kPacksPerThread; ++i) {
       const int c = threadIdx.x + i * blockDim.x;
-      if (c < packs) s[i] = combine_pack<T, kAdd>(s[i], r[i], acc);
+      if (c < packs) {
+        s[i] = combine_pack<T, kAdd>(s[i], r[i], acc);
+        // stored before the reduction (every load of the row precedes it)
+        if constexpr (kAdd) store16(a.residual_output + base + static_cast<int64_t>(c) * E, s[i]);
+      }
     }
     const float inv = inverse_rms(block_allreduce_sum(__fadd_rn(acc.x, acc.y), partial, parity),
                                   n, a.epsilon);
@@ -198,7 +202,6 @@ __global__ void __launch_bounds__(kMaxThreads, kMinBlocks) norm_fp4_cta_kernel(F
       const bool valid = c < packs;
       uint4 y = make_uint4(0, 0, 0, 0);
       if (valid) {
-        if constexpr (kAdd) store16(a.residual_output + base + static_cast<int64_t>(c) * E, s[i]);
         y = normalise_pack<T>(s[i], w[i], inv);
       }
       quantise_fp4_pack<T>(a, row, c, valid, y, g, kTable ? multipliers : nullptr);

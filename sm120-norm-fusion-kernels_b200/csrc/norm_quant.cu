@@ -135,7 +135,11 @@ __global__ void __launch_bounds__(kMaxThreads) norm_quant_cta_kernel(QuantArgs<T
 #pragma unroll
     for (int i = 0; i < kPacksPerThread; ++i) {
       const int c = threadIdx.x + i * blockDim.x;
-      if (c < packs) s[i] = combine_pack<T, kAdd>(s[i], r[i], acc);
+      if (c < packs) {
+        s[i] = combine_pack<T, kAdd>(s[i], r[i], acc);
+        // stored before the reduction (every load of the row precedes it)
+        if constexpr (kAdd) store16(a.residual_output + base + static_cast<int64_t>(c) * E, s[i]);
+      }
     }
     const float inv =
         inverse_rms(block_allreduce(__fadd_rn(acc.x, acc.y), partial, parity, false), n, a.epsilon);
@@ -144,7 +148,6 @@ __global__ void __launch_bounds__(kMaxThreads) norm_quant_cta_kernel(QuantArgs<T
     for (int i = 0; i < kPacksPerThread; ++i) {
       const int c = threadIdx.x + i * blockDim.x;
       if (c < packs) {
-        if constexpr (kAdd) store16(a.residual_output + base + static_cast<int64_t>(c) * E, s[i]);
         s[i] = normalise_pack<T>(s[i], w[i], inv);  // s now holds y
         if constexpr (kDynamic) peak = pack_abs_max<T>(s[i], peak);
       }

@@ -151,6 +151,32 @@ def test_cache_layouts_dtypes_and_strided_views_exact(dtype, layout, cache, stri
             assert_bitwise_equal(g_, w_, what=what)
 
 
+@pytest.mark.parametrize("layout", ["NHD", "HND"])
+@pytest.mark.parametrize("cache", ["same", "fp8"])
+def test_combined_kv_pages(layout, cache):
+    """FlashInfer's paged layout keeps K and V of a page together:
+    [pages, 2, page_size, Hk, D] ("NHD") or [pages, 2, Hk, page_size, D]
+    ("HND"); key_cache = kv[:, 0] and value_cache = kv[:, 1] are strided views
+    (block stride 2 x page), written in place and nothing else."""
+    c = QkCase(torch.bfloat16, 128, 128, tokens=45, layout=layout, cache=cache, seed=11,
+               hq=8, hk=2, blocks=6, block_size=16)
+    want = c.expected()
+    pages = torch.zeros((c.kc.shape[0], 2) + tuple(c.kc.shape[1:]), dtype=c.kc.dtype, device=DEV)
+    kc, vc = pages[:, 0], pages[:, 1]
+    assert not kc.is_contiguous()
+    scales = [s.to(DEV) if s is not None else None for s in (c.k_scale, c.v_scale)]
+    q, k, v = c.q.to(DEV), c.k.to(DEV), c.v.to(DEV)
+    extensions.qk_norm_rope_cache_(q, k, v, c.qw.to(DEV), c.kw.to(DEV), c.pos.to(DEV),
+                                   c.table.to(DEV), kc, vc, c.slots.to(DEV), *scales,
+                                   kv_cache_layout=layout)
+    got = (q.cpu(), k.cpu(), kc.cpu(), vc.cpu())
+    for g_, w_, what in zip(got, want, ("query", "key", "key cache", "value cache")):
+        if g_.dtype in (torch.float8_e4m3fn, torch.uint8):
+            assert torch.equal(g_.contiguous().view(torch.uint8), w_.view(torch.uint8)), what
+        else:
+            assert_bitwise_equal(g_.contiguous(), w_, what=what)
+
+
 @pytest.mark.parametrize("block_size", [1, 5, 16, 32])
 @pytest.mark.parametrize("layout", ["NHD", "HND"])
 def test_block_sizes(block_size, layout):
