@@ -579,6 +579,260 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(4 * kWarpSize, kStag
   }
 }
 
+// ---- Q/K epilogue of one head row on eight lanes -------------------------------
+//
+// For the kernels that finish a head row from a bf16 copy of it in shared
+// memory: eight lanes per row, lane part p holding elements [8p, 8p + 8) and
+// [64 + 8p, 64 + 8p + 8), with head_norm_rope_kernel's sum order, norm,
+// rotation and KV store, so the result is that kernel's on the row. fetch_*
+// are split so that a kernel can issue the loads early.
+struct HeadRow {
+  int64_t position = -1;
+  int64_t slot = -1;
+  bool live = false;
+  bool rope = false;
+  bool norm = false;
+  float2 c[4], sn[4];
+  Half8<__nv_bfloat16> nw_lo{}, nw_hi{};
+};
+
+__device__ __forceinline__ void head_row_fetch_token(HeadRow& r, const GemmArgs& a, bool live,
+                                                     int64_t token) {
+  r.live = live;
+  if (live && a.epilogue) {
+    r.position = a.positions[token];
+    r.slot = a.slots != nullptr ? a.slots[token] : -1;
+  }
+}
+
+__device__ __forceinline__ void head_row_fetch_tables(HeadRow& r, const GemmArgs& a, int head,
+                                                      int part) {
+  if (r.slot >= a.cache_slots) r.slot = -1;
+  r.rope = r.position >= 0 && r.position < a.rope_positions;
+  r.norm = r.live && a.epilogue && r.rope && head < a.query_heads + a.key_heads;
+  if (r.norm) {
+    const int lo = 8 * part;
+    const int hi = kHead / 2 + lo;
+    const __nv_bfloat16* nw = head < a.query_heads ? a.query_weight : a.key_weight;
+    r.nw_lo = load_half<__nv_bfloat16, true>(nw + lo);
+    r.nw_hi = load_half<__nv_bfloat16, true>(nw + hi);
+    load8_pairs<true>(a.cos_sin + r.position * kHead + lo, r.c);
+    load8_pairs<true>(a.cos_sin + r.position * kHead + hi, r.sn);
+  }
+}
+
+// All eight lanes of every group must call (the sum of squares is a shuffle).
+__device__ __forceinline__ void head_row_finish(const HeadRow& r, const GemmArgs& a, int head,
+                                                int64_t token, int part,
+                                                const __nv_bfloat16* row) {
+  const int lo = 8 * part;
+  const int hi = kHead / 2 + lo;
+  Half8<__nv_bfloat16> x_lo{}, x_hi{};
+  if (r.live) {
+    x_lo = load_half<__nv_bfloat16, true>(row + lo);
+    x_hi = load_half<__nv_bfloat16, true>(row + hi);
+  }
+  const float2 sq = half_sum_squares<__nv_bfloat16>(
+      x_hi, half_sum_squares<__nv_bfloat16>(x_lo, make_float2(0.f, 0.f)));
+  const float total = group_allreduce_sum<8>(__fadd_rn(sq.x, sq.y));
+  Half8<__nv_bfloat16> y_lo = x_lo, y_hi = x_hi;
+  if (r.norm) {
+    const float inv = head_inverse_rms<kHead>(make_float2(total, 0.0f), a.epsilon);
+    const Half8<__nv_bfloat16> n_lo = normalise_half<__nv_bfloat16>(x_lo, r.nw_lo, inv);
+    const Half8<__nv_bfloat16> n_hi = normalise_half<__nv_bfloat16>(x_hi, r.nw_hi, inv);
+    rotate_half<__nv_bfloat16>(n_lo, n_hi, r.c, r.sn, y_lo, y_hi);
+  }
+  if (r.live) {
+    __nv_bfloat16* out = a.qkv + token * a.n + static_cast<int64_t>(head) * kHead;
+    store_half<__nv_bfloat16, true>(out + lo, y_lo);
+    store_half<__nv_bfloat16, true>(out + hi, y_hi);
+    if (a.epilogue && r.rope && r.slot >= 0 && head >= a.query_heads) {
+      const bool is_key = head < a.query_heads + a.key_heads;
+      const int kv_head = is_key ? head - a.query_heads : head - a.query_heads - a.key_heads;
+      __nv_bfloat16* cache =
+          (is_key ? a.key_cache : a.value_cache) + (r.slot * a.key_heads + kv_head) * kHead;
+      store_half<__nv_bfloat16, true>(cache + lo, y_lo);
+      store_half<__nv_bfloat16, true>(cache + hi, y_hi);
+    }
+  }
+}
+
+// ---- split K for a few dozen tokens ----------------------------------------
+//
+// Up to 128 tokens give only one 128-token row of one-head tiles (N / 128
+// blocks), each streaming its 128 weight rows through the whole K. Here a
+// cluster of kSplits CTAs shares one such tile: CTA s runs the one-SM main
+// loop (TMA, tcgen05.mma M128 N128 into 128 TMEM columns) over K tiles
+// [s, s + 1) * K / kSplits, copies its fp32 partial tile from TMEM into its
+// shared memory (rows padded to 132 floats: conflict-free 16-byte accesses),
+// and after a cluster barrier CTA s sums rows [s, s + 1) * 128 / kSplits of
+// the kSplits partials, in rank order, through distributed shared memory,
+// rounds them to bf16 and runs the Q/K epilogue on eight lanes per row. Three
+// stages keep two CTAs per SM.
+constexpr int kSplitK = 4;  // CTAs per cluster (measured: 2 and 8 slower)
+constexpr int kSplitRowFloats = kHead + 4;
+constexpr uint32_t kSplitPartialBytes = kTileM * kSplitRowFloats * sizeof(float);
+
+template <int kSplits, int kStages>
+struct SplitShape {
+  static constexpr int kThreads = 4 * kWarpSize;
+  static constexpr uint32_t kStageBytes = 2 * kABytes;  // 128 x 64 of A and of B
+  static constexpr int kRows = kTileM / kSplits;       // rows each CTA finishes
+  static constexpr size_t kSmem =
+      (static_cast<size_t>(kStages) * kStageBytes > kSplitPartialBytes
+           ? static_cast<size_t>(kStages) * kStageBytes
+           : kSplitPartialBytes) + 1024;
+  static constexpr uint32_t kInstrDesc = (1u << 4) | (1u << 7) | (1u << 10) |
+                                         (static_cast<uint32_t>(kHead >> 3) << 17) |
+                                         (static_cast<uint32_t>(kTileM >> 4) << 24);
+  static_assert(kRows * 8 % kThreads == 0, "whole epilogue passes");
+};
+
+template <int kSplits, int kStages>
+__global__ void __launch_bounds__(4 * kWarpSize, 2)
+    qkv_gemm_splitk_kernel(const __grid_constant__ CUtensorMap map_a,
+                           const __grid_constant__ CUtensorMap map_b, GemmArgs a) {
+  namespace cg = cooperative_groups;
+  using S = SplitShape<kSplits, kStages>;
+  extern __shared__ unsigned char dynamic_smem[];
+  __shared__ __align__(8) uint64_t full[kStages];
+  __shared__ __align__(8) uint64_t empty[kStages];
+  __shared__ __align__(8) uint64_t done;
+  __shared__ uint32_t tmem_slot;
+  __shared__ int aborted;
+  __shared__ __align__(16) __nv_bfloat16 rows[S::kRows][kHead];
+  unsigned char* tiles = reinterpret_cast<unsigned char*>(
+      (reinterpret_cast<uintptr_t>(dynamic_smem) + 1023) & ~uintptr_t{1023});
+  float* partial = reinterpret_cast<float*>(tiles);  // after the main loop
+  cg::cluster_group cluster = cg::this_cluster();
+  const int rank = static_cast<int>(cluster.block_rank());
+  const int warp = threadIdx.x / kWarpSize;
+  const int lane = threadIdx.x & (kWarpSize - 1);
+  const int n_tile = blockIdx.x / kSplits;  // = head
+  const int m_tile = blockIdx.y;
+  const int k_count = a.k_tiles / kSplits;
+  const int k_first = rank * k_count;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < kStages; ++s) {
+      mbarrier_init(&full[s], 1);
+      mbarrier_init(&empty[s], 1);
+    }
+    mbarrier_init(&done, 1);
+    aborted = 0;
+    fence_mbarrier_init();
+  }
+  if (warp == 0) tmem_alloc(&tmem_slot, kHead);
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = tmem_slot;
+  wait_for_upstream_grid();
+  release_downstream_grid();
+
+  if (warp == 0 && lane == 0) {
+    for (int k = 0; k < k_count; ++k) {
+      const int s = k % kStages;
+      if (k >= kStages && !wait_or_record(&empty[s], ((k / kStages) - 1) & 1)) {
+        atomicExch(&aborted, 1);
+        break;
+      }
+      if (atomicAdd(&aborted, 0)) break;
+      unsigned char* stage = tiles + static_cast<size_t>(s) * S::kStageBytes;
+      mbarrier_arrive_expect_tx(&full[s], S::kStageBytes);
+      tma_load_2d(stage, &map_a, (k_first + k) * kTileK, m_tile * kTileM, &full[s]);
+      tma_load_2d(stage + kABytes, &map_b, (k_first + k) * kTileK, n_tile * kHead, &full[s]);
+    }
+  } else if (warp == 1 && lane == 0) {
+    for (int k = 0; k < k_count; ++k) {
+      const int s = k % kStages;
+      if (!wait_or_record(&full[s], (k / kStages) & 1)) {
+        atomicExch(&aborted, 1);
+        break;
+      }
+      tc_fence_after();
+      const unsigned char* stage = tiles + static_cast<size_t>(s) * S::kStageBytes;
+      const uint64_t adesc = smem_descriptor(stage);
+      const uint64_t bdesc = smem_descriptor(stage + kABytes);
+#pragma unroll
+      for (int kk = 0; kk < kTileK / kMmaK; ++kk) {
+        mma_bf16(tmem_base, adesc + 2 * kk, bdesc + 2 * kk, S::kInstrDesc, (k | kk) != 0);
+      }
+      mma_commit(&empty[s]);
+    }
+    mma_commit(&done);
+  }
+  __syncwarp();
+
+  // the tokens this CTA finishes: rows rank * kRows .. + kRows of the tile
+  constexpr int kPasses = S::kRows * 8 / S::kThreads;
+  HeadRow job[kPasses];
+#pragma unroll
+  for (int p = 0; p < kPasses; ++p) {
+    const int r = (p * S::kThreads + threadIdx.x) / 8;
+    const int64_t t = static_cast<int64_t>(m_tile) * kTileM + rank * S::kRows + r;
+    head_row_fetch_token(job[p], a, t < a.tokens, t);
+  }
+
+  // this CTA's fp32 partial tile into shared memory (stages are free: every
+  // load was consumed by an MMA that has completed)
+  const bool ready = wait_or_record(&done, 0);
+  tc_fence_after();
+  if (ready) {
+    const int row = warp * kWarpSize + lane;
+    float* dst = partial + row * kSplitRowFloats;
+#pragma unroll 1
+    for (int chunk = 0; chunk < kHead / 32; ++chunk) {
+      uint32_t v[32];
+      tmem_load32(tmem_base + (static_cast<uint32_t>(warp * kWarpSize) << 16) + chunk * 32, v);
+#pragma unroll
+      for (int q = 0; q < 8; ++q) {
+        reinterpret_cast<float4*>(dst + chunk * 32)[q] =
+            make_float4(__uint_as_float(v[4 * q]), __uint_as_float(v[4 * q + 1]),
+                        __uint_as_float(v[4 * q + 2]), __uint_as_float(v[4 * q + 3]));
+      }
+    }
+  }
+#pragma unroll
+  for (int p = 0; p < kPasses; ++p) head_row_fetch_tables(job[p], a, n_tile, lane & 7);
+  cluster.sync();  // every CTA's partial tile is in place
+
+  // sum the partials of this CTA's rows in rank order
+  for (int idx = threadIdx.x; idx < S::kRows * kHead / 4; idx += S::kThreads) {
+    const int r = idx / (kHead / 4);
+    const int col = (idx - r * (kHead / 4)) * 4;
+    const int offset = (rank * S::kRows + r) * kSplitRowFloats + col;
+    float4 sum = *reinterpret_cast<const float4*>(cluster.map_shared_rank(partial + offset, 0));
+#pragma unroll
+    for (int s = 1; s < kSplits; ++s) {
+      const float4 v = *reinterpret_cast<const float4*>(cluster.map_shared_rank(partial + offset, s));
+      sum = make_float4(__fadd_rn(sum.x, v.x), __fadd_rn(sum.y, v.y), __fadd_rn(sum.z, v.z),
+                        __fadd_rn(sum.w, v.w));
+    }
+    reinterpret_cast<uint32_t*>(&rows[r][col])[0] = Pack<__nv_bfloat16>::f32_to_word(sum.x, sum.y);
+    reinterpret_cast<uint32_t*>(&rows[r][col])[1] = Pack<__nv_bfloat16>::f32_to_word(sum.z, sum.w);
+  }
+  __syncthreads();
+  if (ready && !aborted) {
+#pragma unroll
+    for (int p = 0; p < kPasses; ++p) {
+      const int r = (p * S::kThreads + threadIdx.x) / 8;
+      const int64_t t = static_cast<int64_t>(m_tile) * kTileM + rank * S::kRows + r;
+      head_row_finish(job[p], a, n_tile, t, lane & 7, rows[r]);
+    }
+  }
+  tc_fence_before();
+  cluster.sync();  // no CTA leaves while another may still read its partial tile
+  if (warp == 0) {
+    if (!ready) {
+      if (lane == 0) mbarrier_wait_bounded(&done, 0);
+      __syncwarp();
+    }
+    tc_fence_after();
+    tmem_dealloc(tmem_base, kHead);
+  }
+}
+
 // ---- weight streaming for a few tokens -------------------------------------
 //
 // With at most kGemvMaxTokens tokens the projection only has to stream the
@@ -666,14 +920,9 @@ __global__ void __launch_bounds__(kGemvThreads, 3) qkv_gemv_kernel(const __nv_bf
   const int mine = tokens > split ? (tokens - split + splits - 1) / splits : 0;
   const bool epilogue_warp = warp * kWarpSize < mine * 8;
   const int er = threadIdx.x / 8;  // head row of an epilogue lane
-  const bool live = epilogue_warp && er < mine;
   const int et = split + er * splits;
-  int64_t position = -1;
-  int64_t slot = -1;
-  if (live && a.epilogue) {
-    position = a.positions[et];
-    slot = a.slots != nullptr ? a.slots[et] : -1;
-  }
+  HeadRow job;
+  head_row_fetch_token(job, a, epilogue_warp && er < mine, et);
 
   // this thread's rows: 16 warp + 4 i + g; its chunk m of row i sits at
   // ring + (m % kGemvRing) * kGemvPhaseBytes + (i * kGemvThreads + threadIdx.x) * 16.
@@ -752,20 +1001,7 @@ __global__ void __launch_bounds__(kGemvThreads, 3) qkv_gemv_kernel(const __nv_bf
       if (j == 0) partial[t][16 * warp + 4 * i + g] = total;
     }
   }
-  if (slot >= a.cache_slots) slot = -1;
-  const bool rope = position >= 0 && position < a.rope_positions;
-  const bool norm = live && a.epilogue && rope && head < a.query_heads + a.key_heads;
-  const int lo = 8 * j;
-  const int hi = kHead / 2 + lo;
-  float2 c[4], sn[4];
-  Half8<__nv_bfloat16> nw_lo{}, nw_hi{};
-  if (norm) {
-    const __nv_bfloat16* nw = head < a.query_heads ? a.query_weight : a.key_weight;
-    nw_lo = load_half<__nv_bfloat16, true>(nw + lo);
-    nw_hi = load_half<__nv_bfloat16, true>(nw + hi);
-    load8_pairs<true>(a.cos_sin + position * kHead + lo, c);
-    load8_pairs<true>(a.cos_sin + position * kHead + hi, sn);
-  }
+  head_row_fetch_tables(job, a, head, j);
   cluster.sync();  // every CTA's partial sums are in place
 
   // sum the splits' partials of each token this CTA finishes, in rank order
@@ -780,36 +1016,7 @@ __global__ void __launch_bounds__(kGemvThreads, 3) qkv_gemv_kernel(const __nv_bf
   __syncthreads();
 
   // Q/K epilogue, eight lanes per head row (head_norm_rope_kernel's lane map)
-  if (epilogue_warp) {
-    Half8<__nv_bfloat16> x_lo{}, x_hi{};
-    if (live) {
-      x_lo = load_half<__nv_bfloat16, true>(&rows[er][lo]);
-      x_hi = load_half<__nv_bfloat16, true>(&rows[er][hi]);
-    }
-    const float2 sq = half_sum_squares<__nv_bfloat16>(
-        x_hi, half_sum_squares<__nv_bfloat16>(x_lo, make_float2(0.f, 0.f)));
-    const float total = group_allreduce_sum<8>(__fadd_rn(sq.x, sq.y));  // all lanes
-    Half8<__nv_bfloat16> y_lo = x_lo, y_hi = x_hi;
-    if (norm) {
-      const float inv = head_inverse_rms<kHead>(make_float2(total, 0.0f), a.epsilon);
-      const Half8<__nv_bfloat16> n_lo = normalise_half<__nv_bfloat16>(x_lo, nw_lo, inv);
-      const Half8<__nv_bfloat16> n_hi = normalise_half<__nv_bfloat16>(x_hi, nw_hi, inv);
-      rotate_half<__nv_bfloat16>(n_lo, n_hi, c, sn, y_lo, y_hi);
-    }
-    if (live) {
-      __nv_bfloat16* out = a.qkv + static_cast<int64_t>(et) * a.n + static_cast<int64_t>(head) * kHead;
-      store_half<__nv_bfloat16, true>(out + lo, y_lo);
-      store_half<__nv_bfloat16, true>(out + hi, y_hi);
-      if (a.epilogue && rope && slot >= 0 && head >= a.query_heads) {
-        const bool is_key = head < a.query_heads + a.key_heads;
-        const int kv_head = is_key ? head - a.query_heads : head - a.query_heads - a.key_heads;
-        __nv_bfloat16* cache =
-            (is_key ? a.key_cache : a.value_cache) + (slot * a.key_heads + kv_head) * kHead;
-        store_half<__nv_bfloat16, true>(cache + lo, y_lo);
-        store_half<__nv_bfloat16, true>(cache + hi, y_hi);
-      }
-    }
-  }
+  if (epilogue_warp) head_row_finish(job, a, head, et, j, rows[er < mine ? er : 0]);
   cluster.sync();  // no CTA leaves while another may still read its partial sums
 }
 
@@ -879,6 +1086,41 @@ int launch_gemm_pair(const CUtensorMap& map_a, const void* qkv_weight, int64_t n
   const dim3 grid(static_cast<unsigned>(2 * (n / kPairTileN)),
                   static_cast<unsigned>((tokens + kPairTileM - 1) / kPairTileM));
   return launch(kernel, grid, dim3(S::kThreads), S::kSmem, stream, map_a, map_b, a);
+}
+
+template <int kSplits, int kStages>
+int launch_gemm_splitk(const CUtensorMap& map_a, const void* qkv_weight, int64_t n,
+                       int64_t hidden_size, const GemmArgs& a, int64_t tokens, cudaStream_t stream) {
+  using S = SplitShape<kSplits, kStages>;
+  CUtensorMap map_b;
+  int rc = make_map(&map_b, qkv_weight, n, hidden_size, kTileM);
+  if (rc != SM120N_OK) return rc;
+  auto kernel = qkv_gemm_splitk_kernel<kSplits, kStages>;
+  rc = allow_dynamic_smem(reinterpret_cast<const void*>(kernel), S::kSmem);
+  if (rc != SM120N_OK) return rc;
+  cudaLaunchConfig_t config = {};
+  config.gridDim = dim3(static_cast<unsigned>(kSplits * (n / kHead)),
+                        static_cast<unsigned>((tokens + kTileM - 1) / kTileM));
+  config.blockDim = dim3(S::kThreads);
+  config.dynamicSmemBytes = S::kSmem;
+  config.stream = stream;
+  cudaLaunchAttribute attribute[2];
+  attribute[0].id = cudaLaunchAttributeClusterDimension;
+  attribute[0].val.clusterDim.x = kSplits;
+  attribute[0].val.clusterDim.y = 1;
+  attribute[0].val.clusterDim.z = 1;
+  config.attrs = attribute;
+  config.numAttrs = 1;
+  if (programmatic_launch_enabled()) {
+    attribute[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attribute[1].val.programmaticStreamSerializationAllowed = 1;
+    config.numAttrs = 2;
+  }
+  const cudaError_t err = cudaLaunchKernelEx(&config, kernel, map_a, map_b, a);
+  if (err != cudaSuccess) {
+    return fail(SM120N_ERR_CUDA, "kernel launch failed: %s", cudaGetErrorString(err));
+  }
+  return SM120N_OK;
 }
 
 template <int kTokens>
@@ -1067,11 +1309,14 @@ extern "C" int sm120n_qkv_proj_norm_rope_cache(
   // tiles resident at once on the device, a launch takes
   // ceil(tiles / resident) waves, and one 64-element K step of a wave costs
   // about 0.47 us for 128 x 128 tiles (one block per SM, six stages), 0.57 us
-  // for 128 x 256 tiles (one block per SM, four stages) and 0.80 us for
-  // 256 x 256 tiles on CTA pairs (two pairs per two SMs, three stages). The
-  // cheapest estimate wins: 1-384 tokens one-head tiles (1 token 33 us),
-  // 512-768 two-head tiles (512: 42 us against 61 / 47), from 1024 the pairs
-  // (1024: 59 us against 88 / 72; 4096: 163 us against 301 / 197). A pair
+  // for 128 x 256 tiles (one block per SM, four stages), 0.80 us for
+  // 256 x 256 tiles on CTA pairs (two pairs per two SMs, three stages) and,
+  // for one-head tiles split four ways along K (two CTAs per SM), 0.38 us per
+  // step of the whole K. The cheapest estimate wins: 5-128 tokens split K
+  // (16-128 tokens: 24.6-25.4 us against 30.7-32.8 unsplit; two or eight
+  // splits 30-34 us), up to 384 tokens one-head tiles, 512-768 two-head tiles
+  // (512: 42 us against 61 / 47), from 1024 the pairs (1024: 59 us against
+  // 88 / 72; 4096: 163 us against 301 / 197). A pair
   // per 256 x 256 tile with six stages and one pair per two SMs measured
   // 192 us at 4096 tokens: the second resident pair, which overlaps one
   // tile's epilogue with another's main loop, is what the three stages buy.
@@ -1088,6 +1333,12 @@ extern "C" int sm120n_qkv_proj_norm_rope_cache(
   const int64_t cost_one_head = waves(m128 * (n / 128), sms) * 47;
   const int64_t cost_two_heads = waves(m128 * (n / 256), sms) * 57;
   const int64_t cost_pair = waves(m256 * (n / kPairTileN), pairs) * 80;
+  const bool splittable = (hidden_size / kTileK) % kSplitK == 0;
+  const int64_t cost_split =
+      splittable ? waves(m128 * (n / kHead) * kSplitK, 2 * sms) * 38 : INT64_MAX;
+  if (cost_split < cost_one_head && cost_split <= cost_two_heads && cost_split <= cost_pair) {
+    return launch_gemm_splitk<kSplitK, 3>(map_a, qkv_weight, n, hidden_size, a, tokens, st);
+  }
   if (cost_one_head <= cost_two_heads && cost_one_head <= cost_pair) {
     return launch_gemm<128, 6, 4>(map_a, qkv_weight, n, hidden_size, a, tokens, st);
   }
