@@ -43,12 +43,15 @@ def rope_table(positions=4096):
     return torch.cat((f.cos(), f.sin()), dim=-1)
 
 
-# Launch forms (csrc/qkv_gemm.cu): up to eight tokens with hidden a multiple
-# of 512 stream the weights on the CUDA cores (1, 5 and 8 tokens here);
-# otherwise the wave model picks one-head tiles for up to a wave of 128 x 128
-# tiles, two-head tiles next, CTA-pair 256 x 256 tiles for the largest calls.
-# The 1300- and 2048-token cases with 48 heads run on CTA pairs; at 1300
-# tokens the second CTA of the last pair has no token rows.
+# Launch forms (csrc/qkv_gemm.cu): up to four tokens with hidden a multiple
+# of 512 stream the weights on the CUDA cores (the 1-, 2- and 3-token cases
+# here); otherwise a wave model picks 4-way split K over one-head tiles while
+# they fit one wave (e.g. 5, 8, 37, 64, 128 tokens, and 300 tokens with 8
+# heads), plain one-head tiles next (257 tokens with 48 heads), two-head
+# tiles (513, 700, 1000), CTA-pair 256 x 256 tiles for the largest calls
+# (1300 and 2048 tokens with 48 heads; at 1300 tokens the second CTA of the
+# last pair has no token rows). Hidden 64 (K not a multiple of 256) cannot
+# split and runs on one-head tiles.
 @pytest.mark.parametrize("tokens, hidden, hq, hk", [
     (1, 64, 2, 0), (128, 256, 2, 1), (300, 1024, 4, 2), (257, 4096, 32, 8), (1000, 2048, 16, 8),
     (1300, 512, 32, 8), (2048, 1024, 32, 8), (1, 512, 2, 1), (5, 1024, 4, 2), (8, 4096, 32, 8)])
