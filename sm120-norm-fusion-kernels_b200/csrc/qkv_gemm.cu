@@ -668,8 +668,8 @@ __device__ __forceinline__ void head_row_finish(const HeadRow& r, const GemmArgs
 // and after a cluster barrier CTA s sums rows [s, s + 1) * 128 / kSplits of
 // the kSplits partials, in rank order, through distributed shared memory,
 // rounds them to bf16 and runs the Q/K epilogue on eight lanes per row. Three
-// stages keep two CTAs per SM.
-constexpr int kSplitK = 4;  // CTAs per cluster (measured: 2 and 8 slower)
+// stages keep two CTAs per SM (the partial tile and the reduced rows reuse
+// the stage memory).
 constexpr int kSplitRowFloats = kHead + 4;
 constexpr uint32_t kSplitPartialBytes = kTileM * kSplitRowFloats * sizeof(float);
 
@@ -678,10 +678,13 @@ struct SplitShape {
   static constexpr int kThreads = 4 * kWarpSize;
   static constexpr uint32_t kStageBytes = 2 * kABytes;  // 128 x 64 of A and of B
   static constexpr int kRows = kTileM / kSplits;       // rows each CTA finishes
+  // after the main loop the stage memory holds the fp32 partial tile and,
+  // behind it, this CTA's reduced bf16 rows
+  static constexpr size_t kAfterLoop = kSplitPartialBytes + kRows * kHead * 2;
   static constexpr size_t kSmem =
-      (static_cast<size_t>(kStages) * kStageBytes > kSplitPartialBytes
+      (static_cast<size_t>(kStages) * kStageBytes > kAfterLoop
            ? static_cast<size_t>(kStages) * kStageBytes
-           : kSplitPartialBytes) + 1024;
+           : kAfterLoop) + 1024;
   static constexpr uint32_t kInstrDesc = (1u << 4) | (1u << 7) | (1u << 10) |
                                          (static_cast<uint32_t>(kHead >> 3) << 17) |
                                          (static_cast<uint32_t>(kTileM >> 4) << 24);
@@ -700,10 +703,10 @@ __global__ void __launch_bounds__(4 * kWarpSize, 2)
   __shared__ __align__(8) uint64_t done;
   __shared__ uint32_t tmem_slot;
   __shared__ int aborted;
-  __shared__ __align__(16) __nv_bfloat16 rows[S::kRows][kHead];
   unsigned char* tiles = reinterpret_cast<unsigned char*>(
       (reinterpret_cast<uintptr_t>(dynamic_smem) + 1023) & ~uintptr_t{1023});
   float* partial = reinterpret_cast<float*>(tiles);  // after the main loop
+  auto rows = reinterpret_cast<__nv_bfloat16(*)[kHead]>(tiles + kSplitPartialBytes);
   cg::cluster_group cluster = cg::this_cluster();
   const int rank = static_cast<int>(cluster.block_rank());
   const int warp = threadIdx.x / kWarpSize;
@@ -1311,12 +1314,14 @@ extern "C" int sm120n_qkv_proj_norm_rope_cache(
   // about 0.47 us for 128 x 128 tiles (one block per SM, six stages), 0.57 us
   // for 128 x 256 tiles (one block per SM, four stages), 0.80 us for
   // 256 x 256 tiles on CTA pairs (two pairs per two SMs, three stages) and,
-  // for one-head tiles split four ways along K (two CTAs per SM), 0.38 us per
-  // step of the whole K. The cheapest estimate wins: 5-128 tokens split K
-  // (16-128 tokens: 24.6-25.4 us against 30.7-32.8 unsplit; two or eight
-  // splits 30-34 us), up to 384 tokens one-head tiles, 512-768 two-head tiles
-  // (512: 42 us against 61 / 47), from 1024 the pairs (1024: 59 us against
-  // 88 / 72; 4096: 163 us against 301 / 197). A pair
+  // for one-head tiles split along K over a cluster (two CTAs per SM), 0.38
+  // us (four ways) and 0.45 us (two ways) per step of the whole K. The
+  // cheapest estimate wins: 5-128 tokens four-way split K (16-128 tokens:
+  // 24.6-25.4 us against 30.7-32.8 unsplit; eight ways 32.6-33.6 us),
+  // 129-384 two-way split K (256 tokens: 32.7 us, 34.0 us with the Q/K
+  // epilogue, against 34.4 / 36.9 on one-head tiles), 512-768 two-head tiles
+  // (512: 42 us against 61 / 47 / 53 split two ways), from 1024 the pairs
+  // (1024: 59 us against 88 / 72; 4096: 163 us against 301 / 197). A pair
   // per 256 x 256 tile with six stages and one pair per two SMs measured
   // 192 us at 4096 tokens: the second resident pair, which overlaps one
   // tile's epilogue with another's main loop, is what the three stages buy.
@@ -1333,11 +1338,17 @@ extern "C" int sm120n_qkv_proj_norm_rope_cache(
   const int64_t cost_one_head = waves(m128 * (n / 128), sms) * 47;
   const int64_t cost_two_heads = waves(m128 * (n / 256), sms) * 57;
   const int64_t cost_pair = waves(m256 * (n / kPairTileN), pairs) * 80;
-  const bool splittable = (hidden_size / kTileK) % kSplitK == 0;
-  const int64_t cost_split =
-      splittable ? waves(m128 * (n / kHead) * kSplitK, 2 * sms) * 38 : INT64_MAX;
-  if (cost_split < cost_one_head && cost_split <= cost_two_heads && cost_split <= cost_pair) {
-    return launch_gemm_splitk<kSplitK, 3>(map_a, qkv_weight, n, hidden_size, a, tokens, st);
+  const int64_t k_steps = hidden_size / kTileK;
+  const int64_t cost_split4 =
+      k_steps % 4 == 0 ? waves(m128 * (n / kHead) * 4, 2 * sms) * 38 : INT64_MAX;
+  const int64_t cost_split2 =
+      k_steps % 2 == 0 ? waves(m128 * (n / kHead) * 2, 2 * sms) * 45 : INT64_MAX;
+  const int64_t cost_unsplit = std::min({cost_one_head, cost_two_heads, cost_pair});
+  if (cost_split4 < cost_unsplit && cost_split4 <= cost_split2) {
+    return launch_gemm_splitk<4, 3>(map_a, qkv_weight, n, hidden_size, a, tokens, st);
+  }
+  if (cost_split2 < cost_unsplit) {
+    return launch_gemm_splitk<2, 3>(map_a, qkv_weight, n, hidden_size, a, tokens, st);
   }
   if (cost_one_head <= cost_two_heads && cost_one_head <= cost_pair) {
     return launch_gemm<128, 6, 4>(map_a, qkv_weight, n, hidden_size, a, tokens, st);

@@ -54,7 +54,8 @@ def rope_table(positions=4096):
 # split and runs on one-head tiles.
 @pytest.mark.parametrize("tokens, hidden, hq, hk", [
     (1, 64, 2, 0), (128, 256, 2, 1), (300, 1024, 4, 2), (257, 4096, 32, 8), (1000, 2048, 16, 8),
-    (1300, 512, 32, 8), (2048, 1024, 32, 8), (1, 512, 2, 1), (5, 1024, 4, 2), (8, 4096, 32, 8)])
+    (1300, 512, 32, 8), (2048, 1024, 32, 8), (1, 512, 2, 1), (5, 1024, 4, 2), (8, 4096, 32, 8),
+    (2, 8192, 4, 2), (4, 8192, 8, 4)])
 def test_plain_gemm_is_exact_on_exact_inputs(tokens, hidden, hq, hk):
     a, w = operands(tokens, hidden, hq, hk, tokens, exact=True)
     out = torch.zeros(tokens, w.shape[0], device=DEV, dtype=torch.bfloat16)
@@ -80,7 +81,8 @@ def test_plain_gemm_random_inputs_within_one_ulp(tokens, hidden):
 
 @pytest.mark.parametrize("tokens, hidden, hq, hk", [
     (1, 256, 16, 8), (37, 1024, 8, 4), (128, 4096, 32, 8), (700, 2048, 16, 8),
-    (1300, 512, 32, 8), (2048, 1024, 32, 8), (1, 4096, 32, 8), (3, 1024, 8, 4), (8, 512, 16, 8)])
+    (1300, 512, 32, 8), (2048, 1024, 32, 8), (1, 4096, 32, 8), (3, 1024, 8, 4), (8, 512, 16, 8),
+    (4, 8192, 8, 4)])
 @pytest.mark.parametrize("with_cache", [True, False])
 def test_fused_epilogue_equals_gemm_then_qk_kernel(tokens, hidden, hq, hk, with_cache):
     a, w = operands(tokens, hidden, hq, hk, 7 + tokens, exact=False)
