@@ -159,6 +159,7 @@ __global__ void __launch_bounds__(kMaxThreads, kMinBlocks) norm_fp4_cta_kernel(F
   constexpr int E = Pack<T>::kElems;
   __shared__ float partial[2][kWarpSize];
   __shared__ float multipliers[256];
+  prefetch_first_row<T, kAdd>(a, blockIdx.x);  // every NVFP4 row is 16-byte aligned
   wait_for_upstream_grid();
   release_downstream_grid();
   const int packs = a.hidden / E;
@@ -217,6 +218,7 @@ __global__ void __launch_bounds__(1024) norm_fp4_wide_kernel(Fp4Args<T> a) {
   constexpr int E = Pack<T>::kElems;
   __shared__ float partial[2][kWarpSize];
   __shared__ float multipliers[256];
+  prefetch_first_row<T, kAdd>(a, blockIdx.x);  // every NVFP4 row is 16-byte aligned
   wait_for_upstream_grid();
   release_downstream_grid();
   const int packs = a.hidden / E;

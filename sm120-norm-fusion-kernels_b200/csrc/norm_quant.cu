@@ -106,6 +106,8 @@ __global__ void __launch_bounds__(kMaxThreads) norm_quant_cta_kernel(QuantArgs<T
   constexpr int E = Pack<T>::kElems;
   __shared__ float partial[2][kWarpSize];
   __shared__ float peaks[2][kWarpSize];
+  // as in row_norm_cta_kernel: no prefetch for the four-pack (prefill) forms
+  if constexpr (kPacksPerThread < 4) prefetch_first_row<T, kAdd>(a, blockIdx.x);
   wait_for_upstream_grid();
   release_downstream_grid();
   const int packs = a.hidden / E;
