@@ -1144,6 +1144,15 @@ def profile_case(args) -> None:
         out = torch.empty(t, h, device="cuda", dtype=torch.float8_e4m3fn)
         scale = torch.full((1,), 0.05, device="cuda")
         fn = lambda: ext.fused_add_rms_norm_static_fp8_quant(out, x, r, w, scale, EPS)
+    elif args.profile == "fp4":
+        from sm120_rmsnorm import extensions as ext
+        x = torch.randn(t, h, device="cuda", generator=g).to(dt)
+        r = torch.randn(t, h, device="cuda", generator=g).to(dt)
+        w = (1 + 0.1 * torch.randn(h, device="cuda", generator=g)).to(dt)
+        out = torch.empty(t, h // 2, device="cuda", dtype=torch.uint8)
+        scales = torch.empty(ext.nvfp4_scale_bytes(t, h), device="cuda", dtype=torch.uint8)
+        gscale = torch.full((1,), 448.0 * 6.0 / 4.0, device="cuda")
+        fn = lambda: ext.rms_norm_nvfp4_quant(out, scales, x, w, gscale, EPS, r)
     elif args.profile == "projection":
         from sm120_rmsnorm import extensions as ext
         hq, hk = (int(v) for v in args.heads.split(","))
@@ -1217,7 +1226,8 @@ def main():
     parser.add_argument("--skip-cpu", action="store_true")
     parser.add_argument("--step-only", action="store_true",
                         help="run warm-up and the timed steps only (launch-list captures)")
-    parser.add_argument("--profile", choices=["fused", "rms", "qkkv", "qk", "qkcache", "quant", "projection"],
+    parser.add_argument("--profile", choices=["fused", "rms", "qkkv", "qk", "qkcache", "quant", "fp4",
+                                              "projection"],
                         help="launch one operator at one shape and exit (ncu driver)")
     parser.add_argument("--tokens", type=int, default=1024)
     parser.add_argument("--hidden", type=int, default=4096)

@@ -29,6 +29,7 @@
 #include <cuda_fp8.h>
 
 #include <algorithm>
+#include <type_traits>
 
 #include "device_utils.cuh"
 #include "runtime.h"
@@ -86,13 +87,15 @@ __device__ __forceinline__ uint8_t block_scale(float peak, float g) {
 // low Pack<T>::kElems / 2 bytes of the result.
 template <typename T>
 __device__ __forceinline__ uint32_t fp4_pack(const uint4& y, float r) {
-  float f[Pack<T>::kElems];
-  Pack<T>::to_f32(y, f);
+  float2 f[Pack<T>::kElems / 2];
+  pack_to_pairs<T>(y, f);
+  const float2 r2 = make_float2(r, r);
   uint32_t out = 0;
 #pragma unroll
   for (int i = 0; i < Pack<T>::kElems / 2; ++i) {
-    const float2 v = make_float2(__fmul_rn(f[2 * i], r), __fmul_rn(f[2 * i + 1], r));
-    const uint32_t b = __nv_cvt_float2_to_fp4x2(v, __NV_E2M1, cudaRoundNearest);
+    // packed product: each half rounds like __fmul_rn, and only the
+    // conversion consumes it
+    const uint32_t b = __nv_cvt_float2_to_fp4x2(__fmul2_rn(f[i], r2), __NV_E2M1, cudaRoundNearest);
     out |= (b & 0xffu) << (8 * i);
   }
   return out;
@@ -100,12 +103,27 @@ __device__ __forceinline__ uint32_t fp4_pack(const uint4& y, float r) {
 
 template <typename T>
 __device__ __forceinline__ float pack_peak(const uint4& y) {
-  float f[Pack<T>::kElems];
-  Pack<T>::to_f32(y, f);
-  float m = 0.0f;
+  if constexpr (sizeof(T) == 2) {
+    // |y| by clearing the sign bits and the largest by a packed max, both
+    // exact on the 16-bit values
+    using V2 = std::conditional_t<std::is_same_v<T, __half>, __half2, __nv_bfloat162>;
+    auto magnitudes = [](uint32_t w) {
+      w &= 0x7fff7fffu;
+      return *reinterpret_cast<const V2*>(&w);
+    };
+    const V2 m = __hmax2(__hmax2(magnitudes(y.x), magnitudes(y.y)),
+                         __hmax2(magnitudes(y.z), magnitudes(y.w)));
+    float lo, hi;
+    Pack<T>::word_to_f32(*reinterpret_cast<const uint32_t*>(&m), lo, hi);
+    return fmaxf(lo, hi);
+  } else {
+    float f[Pack<T>::kElems];
+    Pack<T>::to_f32(y, f);
+    float m = 0.0f;
 #pragma unroll
-  for (int i = 0; i < Pack<T>::kElems; ++i) m = fmaxf(m, fabsf(f[i]));
-  return m;
+    for (int i = 0; i < Pack<T>::kElems; ++i) m = fmaxf(m, fabsf(f[i]));
+    return m;
+  }
 }
 
 // The largest magnitude of a 16-element block: packs of one block sit in
