@@ -21,10 +21,14 @@
 // Tiling, two SMs per tile (larger token counts): a cluster of two CTAs per
 // 256-token x 256-column tile, tcgen05.mma.cta_group::2 (M 256, N 256), each
 // CTA staging half of A and half of B in three stages, two pairs resident per
-// two SMs (qkv_gemm_pair_kernel below). The host picks the form per call from
-// a measured wave model.
+// two SMs (qkv_gemm_pair_kernel below). Persistent pairs (the fused calls
+// from about 512 tokens): one cluster per two SMs walks the 256 x 256 tiles
+// with warp-specialised loader, tensor-core issuer and four epilogue warps,
+// six stages and two TMEM accumulators, so that each tile's epilogue runs
+// under the next tile's main loop (qkv_gemm_persistent_kernel). The host
+// picks the form per call from a measured wave model.
 //
-// Epilogue: warp w reads TMEM lanes 32w..32w+31, i.e. each thread owns one
+// Epilogue: warp w reads TMEM lanes 32(w % 4) onwards, i.e. each thread owns one
 // token row of the tile and, per head, all 128 accumulators of that row. It
 // rounds them to bf16 (the GEMM output), sums squares in the order the
 // stand-alone Q/K kernel uses (eight 16-element lane slices, pairwise
@@ -579,6 +583,192 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(4 * kWarpSize, kStag
   }
 }
 
+// ---- persistent 2-SM form: warp-specialised, two accumulators ------------------
+//
+// One cluster of two CTAs per pair of SMs walks the 256-token x 256-column
+// tiles tile = cluster, cluster + clusters, ... (column tiles fastest, so
+// the clusters working at once share token rows and the weights stay in L2).
+// Roles: warp 0 lane 0 loads (as in the pair kernel: this CTA's halves of A
+// and B, counted on CTA 0's stage barrier), warp 1 lane 0 of CTA 0 issues
+// the tcgen05.mma.cta_group::2 of every tile, warps 2-5 of both CTAs run the
+// epilogue (warp w reads TMEM lanes 32 (w % 4) onwards). Tensor memory holds
+// two 256-column accumulators: the tensor cores fill one while the epilogue
+// warps drain the other, so a tile's epilogue overlaps the next tile's main
+// loop inside the same CTA (the pair kernel overlaps them only across two
+// resident pairs). Barriers: full / empty per stage as in the pair kernel;
+// acc_full[b] (both CTAs) fires when the tile in accumulator b is complete;
+// acc_empty[b] (CTA 0) counts the eight epilogue warps of the pair that have
+// read accumulator b.
+constexpr int kPersistentStages = 6;
+constexpr int kEpilogueWarps = 4;
+constexpr int kPersistentThreads = (2 + kEpilogueWarps) * kWarpSize;
+constexpr int kAccumulators = 2;
+
+template <int kStages>
+struct PersistentShape {
+  static constexpr int kTmemColumns = kAccumulators * kPairTileN;  // all 512 columns
+  static constexpr size_t kSmem = static_cast<size_t>(kStages) * kPairStageBytes + 1024;
+};
+
+// One arrival on the barrier at `bar`'s offset in CTA `rank` of the cluster.
+__device__ __forceinline__ void mbarrier_arrive_cluster(uint64_t* bar, uint32_t rank) {
+  asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(
+                   peer_shared_address(bar, rank))
+               : "memory");
+}
+
+__device__ __forceinline__ bool flag_set(const int* flag) {
+  return *reinterpret_cast<const volatile int*>(flag) != 0;
+}
+
+template <int kStages>
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPersistentThreads, 1)
+    qkv_gemm_persistent_kernel(const __grid_constant__ CUtensorMap map_a,
+                               const __grid_constant__ CUtensorMap map_b, GemmArgs a,
+                               int column_tiles, int tiles) {
+  using S = PersistentShape<kStages>;
+  extern __shared__ unsigned char dynamic_smem[];
+  __shared__ __align__(8) uint64_t full[kStages];  // used in CTA 0 only
+  __shared__ __align__(8) uint64_t empty[kStages];
+  __shared__ __align__(8) uint64_t acc_full[kAccumulators];
+  __shared__ __align__(8) uint64_t acc_empty[kAccumulators];  // used in CTA 0 only
+  __shared__ __align__(8) uint64_t done;
+  __shared__ uint32_t tmem_slot;
+  __shared__ int aborted;
+  unsigned char* tiles_smem = reinterpret_cast<unsigned char*>(
+      (reinterpret_cast<uintptr_t>(dynamic_smem) + 1023) & ~uintptr_t{1023});
+  const int warp = threadIdx.x / kWarpSize;
+  const int lane = threadIdx.x & (kWarpSize - 1);
+  const uint32_t rank = cluster_rank();
+  const int cluster = static_cast<int>(blockIdx.x / 2);
+  const int clusters = static_cast<int>(gridDim.x / 2);
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < kStages; ++s) {
+      mbarrier_init(&full[s], 1);
+      mbarrier_init(&empty[s], 1);
+    }
+    for (int b = 0; b < kAccumulators; ++b) {
+      mbarrier_init(&acc_full[b], 1);
+      mbarrier_init(&acc_empty[b], 2 * kEpilogueWarps);
+    }
+    mbarrier_init(&done, 1);
+    aborted = 0;
+    fence_mbarrier_init();
+  }
+  if (warp == 1) tmem_alloc_pair(&tmem_slot, S::kTmemColumns);
+  tc_fence_before();
+  cluster_sync();  // barriers of both CTAs initialised, the pair's TMEM allocated
+  tc_fence_after();
+  const uint32_t tmem_base = tmem_slot;
+  wait_for_upstream_grid();
+  release_downstream_grid();
+
+  if (warp == 0) {
+    if (lane == 0) {
+      // loader (both CTAs)
+      int step = 0;
+      for (int tile = cluster; tile < tiles && !flag_set(&aborted); tile += clusters) {
+        const int m_pair = tile / column_tiles;
+        const int n_tile = tile - m_pair * column_tiles;
+        const int64_t first_row = static_cast<int64_t>(m_pair) * kPairTileM + rank * kTileM;
+        // rows past the end load the last token rows (never stored)
+        const int a_row = static_cast<int>(std::min<int64_t>(first_row, a.tokens - 1));
+        const int b_row = n_tile * kPairTileN + static_cast<int>(rank) * kTileM;
+        for (int k = 0; k < a.k_tiles; ++k, ++step) {
+          const int s = step % kStages;
+          if (step >= kStages && !wait_or_record(&empty[s], ((step / kStages) - 1) & 1)) {
+            atomicExch(&aborted, 1);
+            break;
+          }
+          unsigned char* stage = tiles_smem + static_cast<size_t>(s) * kPairStageBytes;
+          if (rank == 0) mbarrier_arrive_expect_tx(&full[s], 2 * kPairStageBytes);
+          const uint32_t bar = peer_shared_address(&full[s], 0);
+          tma_load_2d_pair(stage, &map_a, k * kTileK, a_row, bar);
+          tma_load_2d_pair(stage + kABytes, &map_b, k * kTileK, b_row, bar);
+        }
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0 && rank == 0) {
+      // tensor-core issuer (CTA 0)
+      constexpr uint32_t kInstrDesc = PairShape<3>::kInstrDesc;
+      int step = 0, local = 0;
+      for (int tile = cluster; tile < tiles && !flag_set(&aborted); tile += clusters, ++local) {
+        const int b = local % kAccumulators;
+        if (local >= kAccumulators &&
+            !wait_or_record(&acc_empty[b], ((local / kAccumulators) - 1) & 1)) {
+          atomicExch(&aborted, 1);
+          break;
+        }
+        tc_fence_after();
+        const uint32_t accumulator = tmem_base + static_cast<uint32_t>(b * kPairTileN);
+        bool ok = true;
+        for (int k = 0; k < a.k_tiles; ++k, ++step) {
+          const int s = step % kStages;
+          if (!wait_or_record(&full[s], (step / kStages) & 1)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const unsigned char* stage = tiles_smem + static_cast<size_t>(s) * kPairStageBytes;
+          const uint64_t adesc = smem_descriptor(stage);
+          const uint64_t bdesc = smem_descriptor(stage + kABytes);
+#pragma unroll
+          for (int kk = 0; kk < kTileK / kMmaK; ++kk) {
+            mma_bf16_pair(accumulator, adesc + 2 * kk, bdesc + 2 * kk, kInstrDesc, (k | kk) != 0);
+          }
+          mma_commit_pair(&empty[s]);
+        }
+        if (!ok) {
+          atomicExch(&aborted, 1);
+          break;
+        }
+        mma_commit_pair(&acc_full[b]);  // both CTAs, once this tile's MMAs have completed
+      }
+      mma_commit_pair(&done);
+    }
+  } else {
+    // epilogue (warps 2-5 of both CTAs)
+    const int lane_group = warp % 4;
+    int local = 0;
+    for (int tile = cluster; tile < tiles; tile += clusters, ++local) {
+      const int b = local % kAccumulators;
+      if (!wait_or_record(&acc_full[b], (local / kAccumulators) & 1)) {
+        atomicExch(&aborted, 1);
+        break;
+      }
+      tc_fence_after();
+      const int m_pair = tile / column_tiles;
+      const int n_tile = tile - m_pair * column_tiles;
+      const int64_t first_row = static_cast<int64_t>(m_pair) * kPairTileM + rank * kTileM;
+      store_slab<kPairTileN / kHead, 4>(a, tmem_base + static_cast<uint32_t>(b * kPairTileN),
+                                        lane_group, lane, first_row,
+                                        n_tile * (kPairTileN / kHead));
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbarrier_arrive_cluster(&acc_empty[b], 0);
+    }
+  }
+  __syncwarp();
+
+  // Teardown: every CTA waits (bounded) for the issuer's last commit, which
+  // follows all of the pair's tensor-core work, so no arrival is still on
+  // its way; then no CTA leaves while the other may still signal its
+  // barriers, and the pair's TMEM is released.
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    if (lane == 0) mbarrier_wait_bounded(&done, 0);
+    __syncwarp();
+  }
+  cluster_sync();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc_pair(tmem_base, S::kTmemColumns);
+  }
+}
+
 // ---- Q/K epilogue of one head row on eight lanes -------------------------------
 //
 // For the kernels that finish a head row from a bf16 copy of it in shared
@@ -1091,6 +1281,57 @@ int launch_gemm_pair(const CUtensorMap& map_a, const void* qkv_weight, int64_t n
   return launch(kernel, grid, dim3(S::kThreads), S::kSmem, stream, map_a, map_b, a);
 }
 
+// Clusters of qkv_gemm_persistent_kernel<kStages> resident at once on
+// `device` (the current device; one CTA per SM), cached per device: the
+// runtime's cluster occupancy, at most SMs / 2.
+template <int kStages>
+int persistent_clusters(int device, int sms, int* out) {
+  static std::mutex mutex;
+  static std::map<int, int> cache;
+  std::lock_guard<std::mutex> lock(mutex);
+  auto it = cache.find(device);
+  if (it != cache.end()) {
+    *out = it->second;
+    return SM120N_OK;
+  }
+  using S = PersistentShape<kStages>;
+  auto kernel = qkv_gemm_persistent_kernel<kStages>;
+  int rc = allow_dynamic_smem(reinterpret_cast<const void*>(kernel), S::kSmem);
+  if (rc != SM120N_OK) return rc;
+  cudaLaunchConfig_t config = {};
+  config.gridDim = dim3(static_cast<unsigned>(sms / 2 * 2));
+  config.blockDim = dim3(kPersistentThreads);
+  config.dynamicSmemBytes = S::kSmem;
+  int clusters = 0;
+  const cudaError_t err = cudaOccupancyMaxActiveClusters(&clusters, kernel, &config);
+  if (err != cudaSuccess) {
+    return fail(SM120N_ERR_CUDA, "querying the projection kernel's cluster occupancy failed: %s",
+                cudaGetErrorString(err));
+  }
+  clusters = std::max(1, std::min(clusters, sms / 2));
+  cache[device] = clusters;
+  *out = clusters;
+  return SM120N_OK;
+}
+
+template <int kStages>
+int launch_gemm_persistent(const CUtensorMap& map_a, const void* qkv_weight, int64_t n,
+                           int64_t hidden_size, const GemmArgs& a, int64_t tokens, int clusters,
+                           cudaStream_t stream) {
+  using S = PersistentShape<kStages>;
+  CUtensorMap map_b;
+  int rc = make_map(&map_b, qkv_weight, n, hidden_size, kTileM);
+  if (rc != SM120N_OK) return rc;
+  auto kernel = qkv_gemm_persistent_kernel<kStages>;
+  rc = allow_dynamic_smem(reinterpret_cast<const void*>(kernel), S::kSmem);
+  if (rc != SM120N_OK) return rc;
+  const int column_tiles = static_cast<int>(n / kPairTileN);
+  const int64_t tiles = column_tiles * ((tokens + kPairTileM - 1) / kPairTileM);
+  const int64_t grid_clusters = std::min<int64_t>(tiles, clusters);
+  return launch(kernel, dim3(static_cast<unsigned>(2 * grid_clusters)), dim3(kPersistentThreads),
+                S::kSmem, stream, map_a, map_b, a, column_tiles, static_cast<int>(tiles));
+}
+
 template <int kSplits, int kStages>
 int launch_gemm_splitk(const CUtensorMap& map_a, const void* qkv_weight, int64_t n,
                        int64_t hidden_size, const GemmArgs& a, int64_t tokens, cudaStream_t stream) {
@@ -1308,23 +1549,26 @@ extern "C" int sm120n_qkv_proj_norm_rope_cache(
   int rc = make_map(&map_a, hidden, tokens, hidden_size, kTileM);
   if (rc != SM120N_OK) return rc;
   // The launch form comes from a wave model measured on B200 (Qwen3-8B-shaped
-  // projection, N = 6144, K = 4096, graphs of back-to-back calls): with
-  // tiles resident at once on the device, a launch takes
-  // ceil(tiles / resident) waves, and one 64-element K step of a wave costs
-  // about 0.47 us for 128 x 128 tiles (one block per SM, six stages), 0.57 us
-  // for 128 x 256 tiles (one block per SM, four stages), 0.80 us for
-  // 256 x 256 tiles on CTA pairs (two pairs per two SMs, three stages) and,
-  // for one-head tiles split along K over a cluster (two CTAs per SM), 0.38
-  // us (four ways) and 0.45 us (two ways) per step of the whole K. The
-  // cheapest estimate wins: 5-128 tokens four-way split K (16-128 tokens:
-  // 24.6-25.4 us against 30.7-32.8 unsplit; eight ways 32.6-33.6 us),
-  // 129-384 two-way split K (256 tokens: 32.7 us, 34.0 us with the Q/K
-  // epilogue, against 34.4 / 36.9 on one-head tiles), 512-768 two-head tiles
-  // (512: 42 us against 61 / 47 / 53 split two ways), from 1024 the pairs
-  // (1024: 59 us against 88 / 72; 4096: 163 us against 301 / 197). A pair
-  // per 256 x 256 tile with six stages and one pair per two SMs measured
-  // 192 us at 4096 tokens: the second resident pair, which overlaps one
-  // tile's epilogue with another's main loop, is what the three stages buy.
+  // projection, N = 6144, K = 4096, graphs of back-to-back calls), in ns:
+  // with tiles resident at once on the device, a launch takes
+  // ceil(tiles / resident) waves; one 64-element K step of a wave costs
+  // about 470 ns for 128 x 128 tiles (one block per SM, six stages), 570 for
+  // 128 x 256 tiles (one block per SM, four stages), 850 for 256 x 256 tiles
+  // on CTA pairs (two pairs per two SMs, three stages) and, for one-head
+  // tiles split along K over a cluster (two CTAs per SM), 380 (four ways)
+  // and 450 (two ways) per step of the whole K; the Q/K epilogue adds 3.0,
+  // 5.5, 12, 1.4 and 1.3 us per wave. The persistent pairs take
+  // ceil(tiles / clusters) rounds of 420 ns per K step, plus 5 us of fill
+  // and drain and 6 us for the epilogue of the last tiles (the others
+  // overlap the next tile's main loop). The cheapest estimate wins: 5-128
+  // tokens four-way split K (16-128 tokens: 24.6-25.4 us against 30.7-32.8
+  // unsplit; eight ways 32.6-33.6 us), 129-384 two-way split K (256 tokens:
+  // 32.7 us, 34.0 us with the Q/K epilogue, against 34.4 / 36.9 on one-head
+  // tiles), from 512 tokens the persistent pairs with the Q/K epilogue (512:
+  // 45 us against 47 on two-head tiles; 2048: 92-97 against 125 on pairs;
+  // 4096: 168-175 against 193; 32768: 1188-1202 against 1328), and for the
+  // plain GEMM around 1024 tokens the pairs (55 us against 64: one wave of
+  // pairs against two rounds).
   DeviceInfo dev;
   rc = current_device_info(&dev);
   if (rc != SM120N_OK) return rc;
@@ -1332,28 +1576,44 @@ extern "C" int sm120n_qkv_proj_norm_rope_cache(
   rc = resident_pairs<3>(dev.device, &pairs);
   if (rc != SM120N_OK) return rc;
   const int64_t sms = dev.sm_count;
+  int clusters = 1;
+  rc = persistent_clusters<kPersistentStages>(dev.device, static_cast<int>(sms), &clusters);
+  if (rc != SM120N_OK) return rc;
   const int64_t m128 = (tokens + kTileM - 1) / kTileM;
   const int64_t m256 = (tokens + kPairTileM - 1) / kPairTileM;
-  auto waves = [](int64_t tiles, int64_t slots) { return (tiles + slots - 1) / std::max<int64_t>(slots, 1); };
-  const int64_t cost_one_head = waves(m128 * (n / 128), sms) * 47;
-  const int64_t cost_two_heads = waves(m128 * (n / 256), sms) * 57;
-  const int64_t cost_pair = waves(m256 * (n / kPairTileN), pairs) * 80;
   const int64_t k_steps = hidden_size / kTileK;
+  const int64_t fused = epilogue;
+  auto waves = [](int64_t tiles, int64_t slots) {
+    return (tiles + slots - 1) / std::max<int64_t>(slots, 1);
+  };
+  const int64_t cost_one_head = waves(m128 * (n / 128), sms) * (470 * k_steps + 3000 * fused);
+  const int64_t cost_two_heads = waves(m128 * (n / 256), sms) * (570 * k_steps + 5500 * fused);
+  const int64_t cost_pair =
+      waves(m256 * (n / kPairTileN), pairs) * (850 * k_steps + 12000 * fused);
+  const int64_t cost_persistent =
+      waves(m256 * (n / kPairTileN), clusters) * 420 * k_steps + 5000 + 6000 * fused;
   const int64_t cost_split4 =
-      k_steps % 4 == 0 ? waves(m128 * (n / kHead) * 4, 2 * sms) * 38 : INT64_MAX;
+      k_steps % 4 == 0 ? waves(m128 * (n / kHead) * 4, 2 * sms) * (380 * k_steps + 1400 * fused)
+                       : INT64_MAX;
   const int64_t cost_split2 =
-      k_steps % 2 == 0 ? waves(m128 * (n / kHead) * 2, 2 * sms) * 45 : INT64_MAX;
-  const int64_t cost_unsplit = std::min({cost_one_head, cost_two_heads, cost_pair});
-  if (cost_split4 < cost_unsplit && cost_split4 <= cost_split2) {
+      k_steps % 2 == 0 ? waves(m128 * (n / kHead) * 2, 2 * sms) * (450 * k_steps + 1300 * fused)
+                       : INT64_MAX;
+  const int64_t best = std::min({cost_one_head, cost_two_heads, cost_pair, cost_persistent,
+                                 cost_split4, cost_split2});
+  if (cost_split4 == best) {
     return launch_gemm_splitk<4, 3>(map_a, qkv_weight, n, hidden_size, a, tokens, st);
   }
-  if (cost_split2 < cost_unsplit) {
+  if (cost_split2 == best) {
     return launch_gemm_splitk<2, 3>(map_a, qkv_weight, n, hidden_size, a, tokens, st);
   }
-  if (cost_one_head <= cost_two_heads && cost_one_head <= cost_pair) {
+  if (cost_persistent == best) {
+    return launch_gemm_persistent<kPersistentStages>(map_a, qkv_weight, n, hidden_size, a, tokens,
+                                                     clusters, st);
+  }
+  if (cost_one_head == best) {
     return launch_gemm<128, 6, 4>(map_a, qkv_weight, n, hidden_size, a, tokens, st);
   }
-  if (cost_two_heads <= cost_pair) {
+  if (cost_two_heads == best) {
     return launch_gemm<256, 4, 4>(map_a, qkv_weight, n, hidden_size, a, tokens, st);
   }
   return launch_gemm_pair<3>(map_a, qkv_weight, n, hidden_size, a, tokens, st);

@@ -44,14 +44,17 @@ def rope_table(positions=4096):
 
 
 # Launch forms (csrc/qkv_gemm.cu): up to four tokens with hidden a multiple
-# of 512 stream the weights on the CUDA cores (the 1-, 2- and 3-token cases
-# here); otherwise a wave model picks 4-way split K over one-head tiles while
-# they fit one wave (e.g. 5, 8, 37, 64, 128 tokens, and 300 tokens with 8
-# heads), plain one-head tiles next (257 tokens with 48 heads), two-head
-# tiles (513, 700, 1000), CTA-pair 256 x 256 tiles for the largest calls
-# (1300 and 2048 tokens with 48 heads; at 1300 tokens the second CTA of the
-# last pair has no token rows). Hidden 64 (K not a multiple of 256) cannot
-# split and runs on one-head tiles.
+# of 512 stream the weights on the CUDA cores (the 1-, 2-, 3- and 4-token
+# cases here); otherwise a wave model picks 4-way split K over one-head tiles
+# while they fit one wave (5, 8, 37, 64, 128 tokens, and 300 tokens with 8
+# heads), 2-way split K next (257 tokens with 48 heads), two-head tiles (513,
+# 700, 1000), the persistent CTA pairs with two accumulators for the fused
+# calls from 512 tokens and the larger plain ones (2048 tokens: three rounds
+# of 74 clusters; 512 tokens: fewer tiles than clusters; 4000 tokens with
+# hidden 512: six rounds, so each accumulator cycles three times), and one
+# 256 x 256 tile per CTA pair for plain calls of about a thousand tokens
+# (1300 tokens; the second CTA of the last pair has no token rows). Hidden 64
+# (K not a multiple of 256) cannot split and runs on one-head tiles.
 @pytest.mark.parametrize("tokens, hidden, hq, hk", [
     (1, 64, 2, 0), (128, 256, 2, 1), (300, 1024, 4, 2), (257, 4096, 32, 8), (1000, 2048, 16, 8),
     (1300, 512, 32, 8), (2048, 1024, 32, 8), (1, 512, 2, 1), (5, 1024, 4, 2), (8, 4096, 32, 8),
@@ -82,7 +85,7 @@ def test_plain_gemm_random_inputs_within_one_ulp(tokens, hidden):
 @pytest.mark.parametrize("tokens, hidden, hq, hk", [
     (1, 256, 16, 8), (37, 1024, 8, 4), (128, 4096, 32, 8), (700, 2048, 16, 8),
     (1300, 512, 32, 8), (2048, 1024, 32, 8), (1, 4096, 32, 8), (3, 1024, 8, 4), (8, 512, 16, 8),
-    (4, 8192, 8, 4)])
+    (4, 8192, 8, 4), (257, 4096, 32, 8), (512, 4096, 32, 8), (4000, 512, 32, 8)])
 @pytest.mark.parametrize("with_cache", [True, False])
 def test_fused_epilogue_equals_gemm_then_qk_kernel(tokens, hidden, hq, hk, with_cache):
     a, w = operands(tokens, hidden, hq, hk, 7 + tokens, exact=False)
