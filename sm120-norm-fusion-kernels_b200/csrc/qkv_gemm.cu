@@ -1557,18 +1557,23 @@ extern "C" int sm120n_qkv_proj_norm_rope_cache(
   // on CTA pairs (two pairs per two SMs, three stages) and, for one-head
   // tiles split along K over a cluster (two CTAs per SM), 380 (four ways)
   // and 450 (two ways) per step of the whole K; the Q/K epilogue adds 3.0,
-  // 5.5, 12, 1.4 and 1.3 us per wave. The persistent pairs take
-  // ceil(tiles / clusters) rounds of 420 ns per K step, plus 5 us of fill
-  // and drain and 6 us for the epilogue of the last tiles (the others
-  // overlap the next tile's main loop). The cheapest estimate wins: 5-128
+  // 5.5, 15, 1.4 and 1.3 us per wave. The persistent pairs take
+  // ceil(tiles / clusters) rounds of 420 ns per K step, plus 12 us (fill,
+  // the cold weights, drain) and 3 us for the epilogue of the last tiles
+  // (the others overlap the next tile's main loop). Splitting a last,
+  // partial round into one-head units did not shorten it (1024 tokens:
+  // 63.6 us either way; 4096: 169 against 165): a K step of a unit costs
+  // about the same at N 128 as at N 256. The cheapest estimate wins: 5-128
   // tokens four-way split K (16-128 tokens: 24.6-25.4 us against 30.7-32.8
   // unsplit; eight ways 32.6-33.6 us), 129-384 two-way split K (256 tokens:
   // 32.7 us, 34.0 us with the Q/K epilogue, against 34.4 / 36.9 on one-head
-  // tiles), from 512 tokens the persistent pairs with the Q/K epilogue (512:
-  // 45 us against 47 on two-head tiles; 2048: 92-97 against 125 on pairs;
-  // 4096: 168-175 against 193; 32768: 1188-1202 against 1328), and for the
-  // plain GEMM around 1024 tokens the pairs (55 us against 64: one wave of
-  // pairs against two rounds).
+  // tiles); above that, with the Q/K epilogue, the persistent pairs (512:
+  // 45-47 us against 47 on two-head tiles; 2048: 92-100 against 125-130 on
+  // pairs; 4096: 168-178 against 193-197; 32768: 1188-1231 against 1328;
+  // 1024: 68-70 against 70-75 for one wave of pairs); the plain GEMM takes
+  // two-head tiles at 512-768 tokens, pairs at 1024-1300 and at 4096 (one
+  // wave of pairs against two rounds at 1024: 55-60 against 60-64 us), the
+  // persistent pairs at 2048 and from 8192 tokens.
   DeviceInfo dev;
   rc = current_device_info(&dev);
   if (rc != SM120N_OK) return rc;
@@ -1582,38 +1587,49 @@ extern "C" int sm120n_qkv_proj_norm_rope_cache(
   const int64_t m128 = (tokens + kTileM - 1) / kTileM;
   const int64_t m256 = (tokens + kPairTileM - 1) / kPairTileM;
   const int64_t k_steps = hidden_size / kTileK;
-  const int64_t fused = epilogue;
   auto waves = [](int64_t tiles, int64_t slots) {
     return (tiles + slots - 1) / std::max<int64_t>(slots, 1);
   };
-  const int64_t cost_one_head = waves(m128 * (n / 128), sms) * (470 * k_steps + 3000 * fused);
-  const int64_t cost_two_heads = waves(m128 * (n / 256), sms) * (570 * k_steps + 5500 * fused);
-  const int64_t cost_pair =
-      waves(m256 * (n / kPairTileN), pairs) * (850 * k_steps + 12000 * fused);
-  const int64_t cost_persistent =
-      waves(m256 * (n / kPairTileN), clusters) * 420 * k_steps + 5000 + 6000 * fused;
-  const int64_t cost_split4 =
-      k_steps % 4 == 0 ? waves(m128 * (n / kHead) * 4, 2 * sms) * (380 * k_steps + 1400 * fused)
-                       : INT64_MAX;
-  const int64_t cost_split2 =
-      k_steps % 2 == 0 ? waves(m128 * (n / kHead) * 2, 2 * sms) * (450 * k_steps + 1300 * fused)
-                       : INT64_MAX;
-  const int64_t best = std::min({cost_one_head, cost_two_heads, cost_pair, cost_persistent,
-                                 cost_split4, cost_split2});
-  if (cost_split4 == best) {
+  struct Costs {
+    int64_t one_head, two_heads, pair, persistent, split4, split2;
+  };
+  auto costs = [&](int64_t fused) {
+    Costs c;
+    c.one_head = waves(m128 * (n / 128), sms) * (470 * k_steps + 3000 * fused);
+    c.two_heads = waves(m128 * (n / 256), sms) * (570 * k_steps + 5500 * fused);
+    c.pair = waves(m256 * (n / kPairTileN), pairs) * (850 * k_steps + 15000 * fused);
+    c.persistent = waves(m256 * (n / kPairTileN), clusters) * 420 * k_steps + 12000 + 3000 * fused;
+    c.split4 = k_steps % 4 == 0
+                   ? waves(m128 * (n / kHead) * 4, 2 * sms) * (380 * k_steps + 1400 * fused)
+                   : INT64_MAX;
+    c.split2 = k_steps % 2 == 0
+                   ? waves(m128 * (n / kHead) * 2, 2 * sms) * (450 * k_steps + 1300 * fused)
+                   : INT64_MAX;
+    return c;
+  };
+  // The summation order -- K split four ways, two ways, or not at all --
+  // follows from the plain GEMM's costs, so that a fused call rounds exactly
+  // like the plain GEMM followed by the stand-alone Q/K kernel; the
+  // epilogue's cost then picks among the unsplit forms, which all sum K in
+  // the same order (16-element tensor-core steps, K ascending).
+  const Costs plain = costs(0);
+  const int64_t unsplit = std::min({plain.one_head, plain.two_heads, plain.pair, plain.persistent});
+  if (plain.split4 < unsplit && plain.split4 <= plain.split2) {
     return launch_gemm_splitk<4, 3>(map_a, qkv_weight, n, hidden_size, a, tokens, st);
   }
-  if (cost_split2 == best) {
+  if (plain.split2 < unsplit) {
     return launch_gemm_splitk<2, 3>(map_a, qkv_weight, n, hidden_size, a, tokens, st);
   }
-  if (cost_persistent == best) {
+  const Costs c = epilogue ? costs(1) : plain;
+  const int64_t best = std::min({c.one_head, c.two_heads, c.pair, c.persistent});
+  if (c.persistent == best) {
     return launch_gemm_persistent<kPersistentStages>(map_a, qkv_weight, n, hidden_size, a, tokens,
                                                      clusters, st);
   }
-  if (cost_one_head == best) {
+  if (c.one_head == best) {
     return launch_gemm<128, 6, 4>(map_a, qkv_weight, n, hidden_size, a, tokens, st);
   }
-  if (cost_two_heads == best) {
+  if (c.two_heads == best) {
     return launch_gemm<256, 4, 4>(map_a, qkv_weight, n, hidden_size, a, tokens, st);
   }
   return launch_gemm_pair<3>(map_a, qkv_weight, n, hidden_size, a, tokens, st);

@@ -45,20 +45,24 @@ def rope_table(positions=4096):
 
 # Launch forms (csrc/qkv_gemm.cu): up to four tokens with hidden a multiple
 # of 512 stream the weights on the CUDA cores (the 1-, 2-, 3- and 4-token
-# cases here); otherwise a wave model picks 4-way split K over one-head tiles
-# while they fit one wave (5, 8, 37, 64, 128 tokens, and 300 tokens with 8
-# heads), 2-way split K next (257 tokens with 48 heads), two-head tiles (513,
-# 700, 1000), the persistent CTA pairs with two accumulators for the fused
-# calls from 512 tokens and the larger plain ones (2048 tokens: three rounds
-# of 74 clusters; 512 tokens: fewer tiles than clusters; 4000 tokens with
-# hidden 512: six rounds, so each accumulator cycles three times), and one
-# 256 x 256 tile per CTA pair for plain calls of about a thousand tokens
-# (1300 tokens; the second CTA of the last pair has no token rows). Hidden 64
-# (K not a multiple of 256) cannot split and runs on one-head tiles.
+# cases here); otherwise a wave model picks, from the plain GEMM's costs,
+# 4-way split K over one-head tiles (5, 7, 8, 37, 64, 128 tokens, and 300
+# tokens with 8 heads) or 2-way split K (257 tokens with 48 heads), else an
+# unsplit form by the call's own costs: two-head tiles (513, 700, 1000
+# tokens, fused 1300 x 512), one 256 x 256 tile per CTA pair (plain 1300
+# tokens -- the second CTA of the last pair has no token rows -- and plain
+# 2048 x 1024), or the
+# persistent CTA pairs with two accumulators (plain 2048 x 2048 and 2048 x
+# 4096; fused 2048 x 1024: three rounds of 74 clusters; fused 512 x 4096:
+# fewer tiles than clusters; fused 4000 x 512: six rounds, so each
+# accumulator cycles three times). Fused and plain calls of one shape thus
+# sum K in the same order, which the bit-for-bit comparison below needs.
+# Hidden 64 (K not a multiple of 256) cannot split and runs on one-head
+# tiles.
 @pytest.mark.parametrize("tokens, hidden, hq, hk", [
     (1, 64, 2, 0), (128, 256, 2, 1), (300, 1024, 4, 2), (257, 4096, 32, 8), (1000, 2048, 16, 8),
     (1300, 512, 32, 8), (2048, 1024, 32, 8), (1, 512, 2, 1), (5, 1024, 4, 2), (8, 4096, 32, 8),
-    (2, 8192, 4, 2), (4, 8192, 8, 4)])
+    (2, 8192, 4, 2), (4, 8192, 8, 4), (2048, 2048, 32, 8)])
 def test_plain_gemm_is_exact_on_exact_inputs(tokens, hidden, hq, hk):
     a, w = operands(tokens, hidden, hq, hk, tokens, exact=True)
     out = torch.zeros(tokens, w.shape[0], device=DEV, dtype=torch.bfloat16)
