@@ -177,7 +177,12 @@ __global__ void __launch_bounds__(kMaxThreads, kMinBlocks) norm_fp4_cta_kernel(F
   constexpr int E = Pack<T>::kElems;
   __shared__ float partial[2][kWarpSize];
   __shared__ float multipliers[256];
-  prefetch_first_row<T, kAdd>(a, blockIdx.x);  // every NVFP4 row is 16-byte aligned
+  // every NVFP4 row is 16-byte aligned; the second row only below four packs
+  if constexpr (kPacksPerThread < 4) {
+    prefetch_first_rows<T, kAdd>(a, blockIdx.x, static_cast<int64_t>(blockIdx.x) + gridDim.x);
+  } else {
+    prefetch_first_row<T, kAdd>(a, blockIdx.x);
+  }
   wait_for_upstream_grid();
   release_downstream_grid();
   const int packs = a.hidden / E;

@@ -107,7 +107,9 @@ __global__ void __launch_bounds__(kMaxThreads) norm_quant_cta_kernel(QuantArgs<T
   __shared__ float partial[2][kWarpSize];
   __shared__ float peaks[2][kWarpSize];
   // as in row_norm_cta_kernel: no prefetch for the four-pack (prefill) forms
-  if constexpr (kPacksPerThread < 4) prefetch_first_row<T, kAdd>(a, blockIdx.x);
+  if constexpr (kPacksPerThread < 4) {
+    prefetch_first_rows<T, kAdd>(a, blockIdx.x, static_cast<int64_t>(blockIdx.x) + gridDim.x);
+  }
   wait_for_upstream_grid();
   release_downstream_grid();
   const int packs = a.hidden / E;

@@ -112,7 +112,9 @@ __global__ void __launch_bounds__(kMaxThreads) row_norm_cta_kernel(RowArgs<T> a)
   // Four packs per thread serve the many-row, bandwidth-bound calls, where the
   // prefetch measured neutral and its registers cost the third resident
   // block per SM (695 us against 619 us on 65536 x 8192): they go without it.
-  if constexpr (kPacksPerThread < 4) prefetch_first_row<T, kAdd>(a, blockIdx.x);
+  if constexpr (kPacksPerThread < 4) {
+    prefetch_first_rows<T, kAdd>(a, blockIdx.x, static_cast<int64_t>(blockIdx.x) + gridDim.x);
+  }
   wait_for_upstream_grid();
   release_downstream_grid();
   const int packs = a.hidden / E;
