@@ -116,28 +116,34 @@ __global__ void __launch_bounds__(256, sizeof(T) == 2 ? 5 : 2) head_cache_kernel
   constexpr int kHeadsPerWarp = kWarpSize / kLanes;
   {
     // Before waiting for the upstream grid, ask L2 for the Q / K / V rows of
-    // the tokens in this block's first pass and their positions and slots.
+    // the tokens in this block's first two passes (threads 0-4 and 5-9) and
+    // their positions and slots.
     const uint32_t heads = static_cast<uint32_t>(a.query_heads + a.key_heads);
     const uint32_t units = static_cast<uint32_t>(a.tokens) * heads;
-    const uint32_t first = blockIdx.x * (blockDim.x / kWarpSize) * kHeadsPerWarp;
-    if (first < units && threadIdx.x < 5) {
-      const uint32_t last = min(units, first + (blockDim.x / kWarpSize) * kHeadsPerWarp) - 1;
+    const uint32_t per_block = (blockDim.x / kWarpSize) * kHeadsPerWarp;
+    const uint32_t pass = threadIdx.x / 5;
+    const uint32_t role = threadIdx.x - pass * 5;
+    const uint64_t first_unit =
+        (static_cast<uint64_t>(blockIdx.x) + static_cast<uint64_t>(pass) * gridDim.x) * per_block;
+    if (pass < 2 && first_unit < units) {
+      const uint32_t first = static_cast<uint32_t>(first_unit);
+      const uint32_t last = min(units, first + per_block) - 1;
       const uint32_t t0 = divide(a.heads_div, first);
       const uint32_t t1 = divide(a.heads_div, last);
-      if (kVector && threadIdx.x < 3) {
-        const int count_heads = threadIdx.x == 0 ? a.query_heads : a.key_heads;
-        const T* base = threadIdx.x == 0 ? a.query : threadIdx.x == 1 ? a.key : a.value;
-        const int64_t stride = threadIdx.x == 0 ? a.query_stride
-                             : threadIdx.x == 1 ? a.key_stride : a.value_stride;
-        if (count_heads > 0 && (threadIdx.x < 2 || kCache != kNoCache)) {
+      if (kVector && role < 3) {
+        const int count_heads = role == 0 ? a.query_heads : a.key_heads;
+        const T* base = role == 0 ? a.query : role == 1 ? a.key : a.value;
+        const int64_t stride = role == 0 ? a.query_stride
+                             : role == 1 ? a.key_stride : a.value_stride;
+        if (count_heads > 0 && (role < 2 || kCache != kNoCache)) {
           for (uint32_t t = t0; t <= t1; ++t) {
             prefetch_l2(base + static_cast<int64_t>(t) * stride,
                         static_cast<uint32_t>(count_heads) * D * sizeof(T));
           }
         }
-      } else if (threadIdx.x == 3) {
+      } else if (role == 3) {
         prefetch_l2_line(a.positions + t0);
-      } else if (threadIdx.x == 4 && kCache != kNoCache) {
+      } else if (role == 4 && kCache != kNoCache) {
         prefetch_l2_line(a.slots + t0);
       }
     }

@@ -83,30 +83,37 @@ __global__ void __launch_bounds__(256, sizeof(T) == 2 ? (kHoistWeights ? 4 : 5) 
     head_norm_rope_kernel(HeadArgs<T> a) {
   {
     // Before waiting for the upstream grid, ask L2 for the heads of this
-    // block's first pass and their tokens' position and slot (batch-1 decode:
-    // 1.86 us against 2.11 us; B = 1024: 7.36 against 7.87 us).
+    // block's first two passes (threads 0-4 and 5-9) and their tokens'
+    // position and slot (batch-1 decode: 1.86 us against 2.11 us; B = 1024,
+    // where 540 of 740 blocks make a second pass: 7.36 against 7.87 us with
+    // the first pass alone).
     const uint32_t heads = static_cast<uint32_t>(a.query_heads + a.key_heads);
     const uint32_t units = static_cast<uint32_t>(a.tokens) * heads;
-    const uint32_t first = blockIdx.x * (blockDim.x / kWarpSize) * kHeadsPerWarp;
-    if (first < units && threadIdx.x < 5) {
-      const uint32_t last = min(units, first + (blockDim.x / kWarpSize) * kHeadsPerWarp) - 1;
+    const uint32_t per_block = (blockDim.x / kWarpSize) * kHeadsPerWarp;
+    const uint32_t pass = threadIdx.x / 5;
+    const uint32_t role = threadIdx.x - pass * 5;
+    const uint64_t first_unit =
+        (static_cast<uint64_t>(blockIdx.x) + static_cast<uint64_t>(pass) * gridDim.x) * per_block;
+    if (pass < 2 && first_unit < units) {
+      const uint32_t first = static_cast<uint32_t>(first_unit);
+      const uint32_t last = min(units, first + per_block) - 1;
       const uint32_t t0 = divide(a.heads_div, first);
       const uint32_t count = divide(a.heads_div, last) - t0 + 1;
       if (!kVector) {
         // bulk prefetches need 16-byte-aligned rows
-      } else if (threadIdx.x == 0 && a.query_heads > 0) {
+      } else if (role == 0 && a.query_heads > 0) {
         prefetch_l2(a.query + static_cast<int64_t>(t0) * a.query_heads * kHeadDim,
                     count * a.query_heads * kHeadDim * sizeof(T));
-      } else if (threadIdx.x == 1 && a.key_heads > 0) {
+      } else if (role == 1 && a.key_heads > 0) {
         prefetch_l2(a.key + static_cast<int64_t>(t0) * a.key_heads * kHeadDim,
                     count * a.key_heads * kHeadDim * sizeof(T));
-      } else if (threadIdx.x == 2 && kStoreKV && a.key_heads > 0) {
+      } else if (role == 2 && kStoreKV && a.key_heads > 0) {
         prefetch_l2(a.value + static_cast<int64_t>(t0) * a.key_heads * kHeadDim,
                     count * a.key_heads * kHeadDim * sizeof(T));
       }
-      if (threadIdx.x == 3) {
+      if (role == 3) {
         prefetch_l2_line(a.positions + t0);
-      } else if (threadIdx.x == 4 && kStoreKV) {
+      } else if (role == 4 && kStoreKV) {
         prefetch_l2_line(a.slots + t0);
       }
     }
