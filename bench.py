@@ -1,36 +1,39 @@
 """Benchmark: achieved HBM GB/s (% of B200 peak) and us/call of the fused
 normalisation path, at 1..8 GPUs.
 
-Workload (one "step"): the in-place residual-add + RMSNorm sweep the metric is
-quoted on -- tokens in {1, 4, 16, 64, 256, 1024} x hidden in {768, 1024, 2048,
-4096} x {bf16, fp16}, x and residual ~ N(0, 1), weight ~ N(1, 0.1), eps 1e-6:
-48 calls of ``fused_add_rms_norm_inplace``, replayed as one CUDA graph. L2 is
-flushed (a 512 MiB write) before every timed step, outside the timed events.
-``value`` = algorithmic bytes of all ranks' steps / max-over-ranks device time.
+Headline workload (one "step"): the in-place residual-add + RMSNorm prefill,
+bf16 x and residual [65536, 8192] ~ N(0, 1), weight [8192] ~ N(1, 0.1), eps
+1e-6 -- one call of ``fused_add_rms_norm_inplace`` per step on each GPU's
+share of the rows. Under torchrun the 65536 rows are split evenly across the
+ranks (``sharding.shard_bounds``), so the total problem is fixed as N grows
+(strong scaling) and no collective touches the data path. ``value`` = the
+algorithmic bytes of the whole problem / the max-over-ranks device time per
+step. Each rank's x + residual (2 GiB / N, >= 268 MB at N = 8) is larger than
+L2 (126 MB), so steps run back to back without an L2 flush.
 
-Also reported on the same line:
-  * ``roofline`` -- the dominant kernel of the step (the longest call), its
-    algorithmic bytes per launch over its launch duration, against the
-    measured HBM copy peak. Launch durations (``per_shape``) come from CUDA
-    events around a graph of R back-to-back calls of one shape on R distinct
-    buffer sets (every call reads data that is not in L2), replayed after an
-    L2 flush: duration = replay time / R;
-  * ``e2e`` -- the same sweep through the public API with the inputs copied
-    from pinned host memory and both outputs copied back inside the timed
-    region (one packed upload and one download per step, consecutive steps
-    overlapping on two device buffer sets);
-  * ``per_op`` -- us/call and GB/s of every operator at the other workload
-    shapes (batch-1 and wide-batch decode Q/K norm + RoPE + KV store, the
-    prefill fused add [65536, 8192] and Q/K prefill of 32768 tokens, and the
-    fp32 RMSNorm rows), timed the same way as ``per_shape``;
-  * ``cpu_baseline`` -- the C oracle on the host cores (rank 0, N=1 only).
+Also on the line:
+  * ``roofline`` -- the headline kernel (one launch per step): algorithmic
+    bytes per launch over its launch duration, against the measured HBM copy
+    peak; its ``per_config`` table covers every workload configuration
+    (us/call, GB/s, fraction of peak, strong-scaling data for the sharded
+    ones, and comparators at N = 1), and ``repeat`` the headline measured in
+    5 independent processes x 3 samples (N = 1);
+  * ``e2e`` -- the headline through the public API with x and residual
+    uploaded from pinned host memory and both results downloaded, every step,
+    inside the timed region;
+  * ``cpu_baseline`` -- the C restatement of the reference's CPU path on the
+    host cores (rank 0, N = 1 only), on a bounded sample of the workload.
+
+Per-config timing: a CUDA graph of R back-to-back calls on R distinct buffer
+sets (R <= 64, at most 256 MiB in all, so every call reads data that is not
+in L2), replayed after an L2 flush (a 512 MiB write, outside the timed
+events); us/call = replay time / R.
 
 ``--impl reference`` times the reference path's CPU implementation (the C
-restatement of its PyTorch oracle) on the host cores instead.
-
-Multi-GPU: launched one process per GPU by torchrun; each rank runs the same
-per-rank workload on its own GPU (rows / sequences sharded, no collective on
-the data path). NCCL is used only for the barrier and the max-over-ranks time.
+restatement of its PyTorch oracle, all host threads) on the headline workload
+in 5 independent processes, and the reference's own CUDA kernels on the same
+workload on this GPU. ``--detail FILE`` also runs the engine-side extension,
+engine and projection suites and writes them to FILE.
 """
 from __future__ import annotations
 
@@ -56,6 +59,12 @@ DTYPES = {"bf16": torch.bfloat16, "fp16": torch.float16}
 EPS = 1e-6
 FLUSH_BYTES = 512 * 1024 * 1024
 FALLBACK_HBM_GBS = 6650.0
+HEADLINE_ROWS, HEADLINE_HIDDEN = 65536, 8192
+HEADLINE_WORKLOAD = ("in-place residual add + RMSNorm prefill, bf16 x and residual "
+                     "[65536, 8192] ~ N(0,1), weight ~ N(1,0.1), eps 1e-6; rows split evenly "
+                     "across the GPUs")
+METRIC = "achieved HBM GB/s (% of B200 peak) and us/call per op at 1/2/4/8 GPUs"
+REPEAT_PROCESSES, REPEAT_SAMPLES = 5, 3
 
 
 # ---------------------------------------------------------------------------
@@ -75,8 +84,18 @@ def qk_kv_bytes(t: int, hq: int, hk: int, s: int, d: int = 128) -> int:
     return t * (s * d * (2 * hq + 5 * hk) + 8 + 4 + 4 * d) + 2 * d * s
 
 
+def qk_bytes(t: int, hq: int, hk: int, s: int, d: int = 128) -> int:
+    # q, k read + written; position and one cos/sin row per token; weights once
+    return t * (s * d * (2 * hq + 2 * hk) + 8 + 4 * d) + 2 * d * s
+
+
 def sweep_shapes():
     return [(t, h, name) for name in DTYPES for t in TOKENS for h in HIDDEN]
+
+
+def shard_bounds(total: int, world: int, rank: int) -> tuple[int, int]:
+    from sm120_rmsnorm.sharding import shard_bounds as bounds
+    return bounds(total, world, rank)
 
 
 # ---------------------------------------------------------------------------
@@ -95,7 +114,7 @@ class Dist:
 
             import torch.distributed as dist
             torch.cuda.set_device(self.local_rank)
-            dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+            dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
                                     device_id=torch.device("cuda", self.local_rank))
             self.pg = dist
         else:
@@ -128,9 +147,10 @@ def measured_hbm_peak():
         return FALLBACK_HBM_GBS, "fallback (6.65 TB/s pool figure; MEASURED_PEAKS.json absent)"
 
 
-def dram_traffic_per_launch():
-    """dram bytes read + written per launch of the dominant kernel, from the
-    committed ncu summary (profiles/dram_traffic.txt), or None."""
+def dram_traffic_per_launch(rows: int):
+    """DRAM bytes read + written by one launch of the headline kernel on `rows`
+    rows, scaled by rows from the committed ncu capture of a smaller launch of
+    the same kernel (profiles/dram_traffic.txt), or None."""
     path = ROOT / "profiles" / "dram_traffic.txt"
     if not path.exists():
         return None
@@ -139,7 +159,14 @@ def dram_traffic_per_launch():
         if "=" in line and not line.startswith("#"):
             k, v = line.split("=", 1)
             out[k.strip()] = v.strip()
-    return out
+    try:
+        captured_rows = int(out["rows"])
+        per_launch = float(out["dram_bytes_per_launch"])
+    except (KeyError, ValueError):
+        return None
+    if out.get("hidden") != str(HEADLINE_HIDDEN):
+        return None
+    return int(per_launch * rows / captured_rows)
 
 
 def sampled_gpus(world: int) -> str:
@@ -212,7 +239,7 @@ class ClockSampler:
 
 
 # ---------------------------------------------------------------------------
-# GPU arm
+# timing helpers
 # ---------------------------------------------------------------------------
 class Flusher:
     def __init__(self):
@@ -228,7 +255,7 @@ def event_pair():
 
 def capture(fns):
     """A CUDA graph of the calls in `fns` (each run once first, so lazy kernel
-    loading stays out of it)."""
+    loading and compilation stay out of it)."""
     for fn in fns:
         fn()
     torch.cuda.synchronize()
@@ -254,150 +281,95 @@ def time_graph(graph, flush: "Flusher", reps: int) -> float:
     return total / reps
 
 
-class SweepData:
-    def __init__(self, seed: int):
-        g = torch.Generator(device="cuda").manual_seed(seed)
-        self.items = []
-        for t, h, name in sweep_shapes():
-            dt = DTYPES[name]
-            x = torch.randn(t, h, device="cuda", generator=g).to(dt)
-            r = torch.randn(t, h, device="cuda", generator=g).to(dt)
-            w = (1.0 + 0.1 * torch.randn(h, device="cuda", generator=g)).to(dt)
-            self.items.append((t, h, name, x, r, w))
-        self.bytes = sum(fused_bytes(t, h, x.element_size()) for t, h, _, x, _, _ in self.items)
-
-    def run(self, ops):
-        for _, _, _, x, r, w in self.items:
-            ops.fused_add_rms_norm_inplace(x, r, w, EPS)
-
-
-def per_shape_times(ops, data: "SweepData", flush: "Flusher", dist: "Dist", args) -> list:
-    """Per-launch duration of every sweep shape: a graph of R back-to-back calls
-    on R distinct buffer sets (every call reads data that is not in L2),
-    replayed after an L2 flush; duration = replay time / R."""
-    per_shape = []
-    g = torch.Generator(device="cuda").manual_seed(77 + dist.rank)
-    for t, h, name, x, r, w in data.items:
-        nbytes = fused_bytes(t, h, x.element_size())
-        sets = max(1, min(64, (256 << 20) // nbytes))
-        bufs = [(x, r)] + [(torch.randn(t, h, device="cuda", generator=g).to(x.dtype),
-                            torch.randn(t, h, device="cuda", generator=g).to(x.dtype))
-                           for _ in range(sets - 1)]
-        calls = [(lambda bx=bx, br=br, w=w: ops.fused_add_rms_norm_inplace(bx, br, w, EPS))
-                 for bx, br in bufs]
-        shape_graph, _ = capture(calls)
-        us = time_graph(shape_graph, flush, max(3, args.reps)) / sets
-        del shape_graph, bufs, calls
-        per_shape.append({"tokens": t, "hidden": h, "dtype": name, "us": round(dist.max(us), 3),
-                          "bytes": nbytes, "calls_per_graph": sets})
-    for p in per_shape:
-        p["gbs"] = round(p["bytes"] / (p["us"] * 1e-6) / 1e9, 1)
-    return per_shape
-
-
-def sweep_step_ms(ops, data: "SweepData", flush: "Flusher", steps: int, warmup: int,
-                  dist: "Dist") -> float:
-    """Mean device time of one step (the 48-call sweep as one CUDA graph), L2
-    flushed before every step outside the timed events."""
-    graph, _ = capture([lambda: data.run(ops)])
-    for _ in range(warmup):
-        flush()
-        graph.replay()
-    dist.barrier()
-    pairs = []
-    for _ in range(steps):
-        flush()
-        a, b = event_pair()
-        a.record()
-        graph.replay()
-        b.record()
-        pairs.append((a, b))
-    dist.barrier()
-    return sum(a.elapsed_time(b) for a, b in pairs) / steps
-
-
-def gpu_arm(args, dist: Dist) -> dict:
-    import sm120_rmsnorm as ops
-
-    dev = torch.device("cuda", torch.cuda.current_device())
-    flush = Flusher()
-    data = SweepData(seed=1234 + dist.rank)
-
-    launches_per_step = len(data.items)
-    clocks = ClockSampler(sampled_gpus(dist.world) if dist.rank == 0 else None)
-    clocks.__enter__()
+def time_calls(calls, flush: "Flusher", reps: int) -> tuple[float, str]:
+    """us per call of `calls` (R calls on R distinct buffer sets) by the graph
+    protocol; calls that cannot be captured in a CUDA graph (some library
+    comparators) are timed as an eager back-to-back loop after the same flush."""
     try:
-        step_ms = sweep_step_ms(ops, data, flush, args.steps, args.warmup, dist)
-        if args.step_only:  # the timed steps alone (for a launch-list capture)
-            return {"metric": "step only", "ms_per_step": round(dist.max(step_ms), 5),
-                    "gpu_launches": launches_per_step * args.steps}
-        line = _measure_rest(args, dist, ops, flush, data, step_ms, launches_per_step)
-    finally:
-        clocks.__exit__(None, None, None)
-    line["clocks"] = clocks.summary() if dist.rank == 0 else None
-    return line
+        graph, _ = capture(calls)
+    except Exception:  # noqa: BLE001 - comparators only; our own calls capture
+        torch.cuda.synchronize()
+        total = 0.0
+        for _ in range(reps):
+            flush()
+            a, b = event_pair()
+            a.record()
+            for fn in calls:
+                fn()
+            b.record()
+            b.synchronize()
+            total += a.elapsed_time(b) * 1e3
+        return total / reps / len(calls), "eager loop"
+    us = time_graph(graph, flush, reps) / len(calls)
+    del graph
+    return us, "graph"
 
 
-def _measure_rest(args, dist, ops, flush, data, step_ms, launches_per_step) -> dict:
-    dev = torch.device("cuda", torch.cuda.current_device())
-    step_ms_max = dist.max(step_ms)
-    value = data.bytes * dist.world / (step_ms_max * 1e-3) / 1e9
+def sets_for(nbytes: int) -> int:
+    """Distinct buffer sets per timed graph: up to 64, at most 256 MiB in all."""
+    return max(1, min(64, (256 << 20) // max(nbytes, 1)))
 
-    per_shape = per_shape_times(ops, data, flush, dist, args)
-    for p in per_shape:
-        p["gbs"] = round(p["bytes"] / (p["us"] * 1e-6) / 1e9, 1)
-    dominant = max(per_shape, key=lambda p: p["us"])
-    peak, peak_source = measured_hbm_peak()
-    traffic = dram_traffic_per_launch()
-    traffic_value = None
-    if traffic and traffic.get("config") == \
-            f"fused_add_rms_norm_inplace {dominant['tokens']}x{dominant['hidden']}":
-        traffic_value = int(float(traffic.get("dram_bytes_per_launch", "nan")))
-    roofline = {"bound": "hbm", "achieved": dominant["gbs"], "peak": peak, "unit": "GB/s",
-                "frac": round(dominant["gbs"] / peak, 4), "traffic": traffic_value,
-                "kernel": f"fused_add_rms_norm_inplace {dominant['dtype']} "
-                          f"{dominant['tokens']}x{dominant['hidden']}",
-                "timing": "CUDA events around a graph of R back-to-back calls of this "
-                          "shape on R distinct buffer sets, replayed after an L2 flush; "
-                          "duration = replay time / R",
-                "algorithmic_bytes_per_launch": dominant["bytes"],
-                "launch_us": dominant["us"], "peak_source": peak_source + ", of measured"
-                if peak_source.startswith("measured") else peak_source + ", of fallback"}
 
-    # end to end through the public API with pinned host buffers. Every step
-    # uploads the step's inputs (each call's x and r, packed 256-byte aligned
-    # in one pinned host buffer) in one copy, runs the 48 calls on views of
-    # the device copy and downloads the results in one copy. Consecutive steps
-    # rotate over three device buffer sets, so step k + 1's upload runs while
-    # step k computes and downloads and no upload waits for a compute
-    # (uploads, calls and downloads on three streams; both PCIe directions
-    # busy), as a streaming engine would.
-    # E steps are captured as one CUDA graph and the graph is timed; per-step
-    # time = elapsed / E.
-    offsets, total = [], 0
-    for _, _, _, x, r, _ in data.items:
-        nb = x.numel() * x.element_size()
-        offsets.append((total, total + ((nb + 255) // 256) * 256, nb))
-        total += 2 * ((nb + 255) // 256) * 256
-    host_in = torch.empty(total, dtype=torch.uint8).pin_memory()
-    host_out = torch.empty(total, dtype=torch.uint8).pin_memory()
-    for (ox, orr, nb), (_, _, _, x, r, _) in zip(offsets, data.items):
-        host_in[ox:ox + nb].copy_(x.reshape(-1).view(torch.uint8).cpu())
-        host_in[orr:orr + nb].copy_(r.reshape(-1).view(torch.uint8).cpu())
+def rope_table(n: int, rotary: int = 128, device="cuda", dtype=torch.float32):
+    inv = 1.0 / (1e6 ** (torch.arange(0, rotary, 2, dtype=torch.float32, device=device) / rotary))
+    f = torch.outer(torch.arange(n, dtype=torch.float32, device=device), inv)
+    return torch.cat((f.cos(), f.sin()), dim=-1).to(dtype)
+
+
+# ---------------------------------------------------------------------------
+# headline: the prefill residual add + RMSNorm, rows sharded over the ranks
+# ---------------------------------------------------------------------------
+class PrefillRows:
+    """This rank's rows of the headline workload on its GPU."""
+
+    def __init__(self, rows: int, seed: int, device="cuda"):
+        g = torch.Generator(device=device).manual_seed(seed)
+        h = HEADLINE_HIDDEN
+        self.rows = rows
+        self.x = torch.randn(rows, h, device=device, generator=g).to(torch.bfloat16)
+        self.r = torch.randn(rows, h, device=device, generator=g).to(torch.bfloat16)
+        self.w = (1 + 0.1 * torch.randn(h, device=device, generator=g)).to(torch.bfloat16)
+        self.bytes = fused_bytes(rows, h, 2)
+
+    def call(self, ops):
+        ops.fused_add_rms_norm_inplace(self.x, self.r, self.w, EPS)
+
+
+def headline_step_ms(ops, head: PrefillRows, steps: int, warmup: int, dist: "Dist") -> float:
+    """Device time per step (one call on this rank's rows), CUDA events around
+    exactly `steps` back-to-back calls, barrier + synchronize on both sides."""
+    for _ in range(warmup):
+        head.call(ops)
+    dist.barrier()
+    a, b = event_pair()
+    a.record()
+    for _ in range(steps):
+        head.call(ops)
+    b.record()
+    dist.barrier()
+    return a.elapsed_time(b) / steps
+
+
+def e2e_headline(ops, head: PrefillRows, steps: int, dist: "Dist") -> dict:
+    """The headline through sm120_rmsnorm.fused_add_rms_norm_inplace with host
+    buffers: every step uploads this rank's x and residual (one packed pinned
+    buffer, one copy), runs the call on views of the device copy and downloads
+    both results (one copy). Three device buffer sets rotate over three
+    streams, so a step's upload overlaps the previous step's call and
+    download; per-step time = elapsed / steps (max over ranks)."""
+    n = head.x.numel() * head.x.element_size()
+    total = 2 * n
+    host_in = torch.empty(total, dtype=torch.uint8, pin_memory=True)
+    host_out = torch.empty(total, dtype=torch.uint8, pin_memory=True)
+    host_in[:n].view(torch.bfloat16).copy_(head.x.view(-1))
+    host_in[n:].view(torch.bfloat16).copy_(head.r.view(-1))
     dev_sets = [torch.empty(total, dtype=torch.uint8, device="cuda") for _ in range(3)]
-
-    def views(buf):
-        out = []
-        for (ox, orr, nb), (t, h, _, x, _, w) in zip(offsets, data.items):
-            out.append((buf[ox:ox + nb].view(x.dtype).view(t, h),
-                        buf[orr:orr + nb].view(x.dtype).view(t, h), w))
-        return out
-
-    set_views = [views(b) for b in dev_sets]
-    h2d = total
+    shape = (head.rows, HEADLINE_HIDDEN)
+    views = [(b[:n].view(torch.bfloat16).view(shape), b[n:].view(torch.bfloat16).view(shape))
+             for b in dev_sets]
     up, compute, down = torch.cuda.Stream(), torch.cuda.Stream(), torch.cuda.Stream()
 
-    def e2e_steps_run(n_steps):
+    def run(n_steps):
         origin = torch.cuda.current_stream()
         for stream in (up, compute, down):
             stream.wait_stream(origin)
@@ -412,8 +384,8 @@ def _measure_rest(args, dist, ops, flush, data, step_ms, launches_per_step) -> d
                 uploaded.record(up)
             compute.wait_event(uploaded)
             with torch.cuda.stream(compute):
-                for x, r, w in set_views[i]:
-                    ops.fused_add_rms_norm_inplace(x, r, w, EPS)
+                x, r = views[i]
+                ops.fused_add_rms_norm_inplace(x, r, head.w, EPS)
                 computed = torch.cuda.Event()
                 computed.record(compute)
             down.wait_event(computed)
@@ -424,149 +396,54 @@ def _measure_rest(args, dist, ops, flush, data, step_ms, launches_per_step) -> d
         for stream in (up, compute, down):
             origin.wait_stream(stream)
 
-    e2e_steps = max(6, args.steps // 5)
-    e2e_steps_run(3)  # eager once, then capture
-    torch.cuda.synchronize()
-    e2e_graph = torch.cuda.CUDAGraph()
-    with torch.cuda.graph(e2e_graph):
-        e2e_steps_run(e2e_steps)
-    for _ in range(max(1, args.warmup // 2)):
-        e2e_graph.replay()
+    run(2)  # warm-up
+    e2e_steps = max(6, steps // 2)
     dist.barrier()
     a, b = event_pair()
     a.record()
-    e2e_graph.replay()
+    run(e2e_steps)
     b.record()
-    b.synchronize()
-    e2e_ms = dist.max(a.elapsed_time(b) / e2e_steps)
-    e2e = {"value": round(data.bytes * dist.world / (e2e_ms * 1e-3) / 1e9, 2), "unit": "GB/s",
-           "ms_per_step": round(e2e_ms, 4), "h2d_bytes_per_step": h2d * dist.world,
-           "d2h_bytes_per_step": h2d * dist.world,
-           "path": "sm120_rmsnorm.fused_add_rms_norm_inplace on views of one packed device "
-                   "buffer per step: one pinned-host upload and one download per step, three "
-                   "device buffer sets in rotation so that a step's upload overlaps the "
-                   "previous step's calls and download (three streams), "
-                   f"{e2e_steps} steps per CUDA graph"}
-
-    per_op = {} if args.skip_per_op else per_op_suite(ops, flush, dist, args)
-    extensions = {} if args.skip_per_op else extension_suite(flush, dist, args)
-    engine = {} if args.skip_per_op else engine_suite(flush, dist, args)
-    projection = {} if args.skip_per_op else projection_suite(flush, dist, args)
-
-    return {
-        "metric": "achieved HBM GB/s (% of B200 peak) and us/call per op at 1/2/4/8 GPUs",
-        "value": round(value, 2), "unit": "GB/s", "n_gpus": dist.world, "steps": args.steps,
-        "warmup": args.warmup, "ms_per_step": round(step_ms_max, 5), "higher_is_better": True,
-        "scaling": "weak", "vs_baseline": None, "dtype": "bf16+fp16 (fp32 accumulate)",
-        "data": "synthetic (seeded N(0,1) activations, N(1,0.1) weights)",
-        "config": {"workload": "in-place residual add + RMSNorm sweep: tokens "
-                               "{1,4,16,64,256,1024} x hidden {768,1024,2048,4096} x "
-                               "{bf16,fp16}, one CUDA graph of 48 launches per step",
-                   "global_batch": len(data.items) * dist.world,
-                   "bytes_per_step_per_gpu": data.bytes, "parallelism": f"dp{dist.world}"
-                   f" (each rank its own rows, no collective)",
-                   "l2": "flushed (512 MiB write) before every timed step and every "
-                         "per-launch timing, outside the events"},
-        "roofline": roofline, "e2e": e2e, "gpu_launches": launches_per_step * args.steps,
-        "per_shape": per_shape, "per_op": per_op, "extensions": extensions, "engine": engine,
-        "projection": projection,
-        "device": torch.cuda.get_device_name(dev),
-    }
+    dist.barrier()
+    ms = dist.max(a.elapsed_time(b) / e2e_steps)
+    del dev_sets, views, host_in, host_out
+    torch.cuda.empty_cache()
+    return {"value": round(fused_bytes(HEADLINE_ROWS, HEADLINE_HIDDEN, 2) / (ms * 1e-3) / 1e9, 2),
+            "unit": "GB/s", "ms_per_step": round(ms, 3),
+            "h2d_bytes_per_step": total * dist.world, "d2h_bytes_per_step": total * dist.world,
+            "path": "sm120_rmsnorm.fused_add_rms_norm_inplace on views of one packed device "
+                    "buffer per step and rank: one pinned-host upload of x and residual and one "
+                    "download of both results per step, three device buffer sets rotating over "
+                    f"three streams, {e2e_steps} steps timed"}
 
 
-def per_op_suite(ops, flush: Flusher, dist: Dist, args) -> dict:
-    """us/call and GB/s of each operator at the other workload shapes.
+# ---------------------------------------------------------------------------
+# comparators (N = 1 only; never on the product path)
+# ---------------------------------------------------------------------------
+class ReferenceKernels:
+    """The reference project's own CUDA kernels (compiled for sm_100a from its
+    sources by oracle/build_ref.py), called with its ops.py default versions."""
 
-    Each entry is a CUDA graph of R back-to-back calls on R distinct buffer
-    sets (R up to 64, fewer when a call moves more than 4 MiB), replayed after
-    an L2 flush, so every call reads inputs that are not in L2; us/call is the
-    replay time over R.
-    """
-    out = {}
-    reps = max(3, args.reps)
-    g = torch.Generator(device="cuda").manual_seed(99 + dist.rank)
-    cpu_g = torch.Generator().manual_seed(7 + dist.rank)
-    bf = torch.bfloat16
+    def __init__(self, module):
+        self.m = module
 
-    def rope_cache(n):
-        inv = 1.0 / (1e6 ** (torch.arange(0, 128, 2, dtype=torch.float32, device="cuda") / 128))
-        f = torch.outer(torch.arange(n, dtype=torch.float32, device="cuda"), inv)
-        return torch.cat((f.cos(), f.sin()), dim=-1)
+    @classmethod
+    def load(cls):
+        from oracle import build_ref
+        module = build_ref.load()
+        return None if module is None else cls(module)
 
-    cache = rope_cache(32768)
+    def fused_add_rms_norm_inplace(self, x, r, w, eps=EPS, version=0):
+        self.m.fused_add_rms_norm_inplace(x, r, w, eps, version)
 
-    def sets_for(nbytes):
-        return max(1, min(64, (256 << 20) // max(nbytes, 1)))
+    def rms_norm_out(self, x, w, out, eps=EPS, version=2):
+        self.m.rms_norm_out(x, w, out, eps, version)
 
-    def record(name, calls, nbytes):
-        graph, _ = capture(calls)
-        us = dist.max(time_graph(graph, flush, reps) / len(calls))
-        out[name] = {"us": round(us, 3), "bytes": nbytes,
-                     "gbs": round(nbytes / (us * 1e-6) / 1e9, 1), "calls_per_graph": len(calls)}
-        del graph
+    def fused_qk_rms_norm_rope(self, q, k, qw, kw, pos, cache, eps=EPS, version=2):
+        self.m.fused_qk_rms_norm_rope(q, k, qw, kw, pos, cache, eps, version)
 
-    # fp32 RMSNorm rows of 1024 (the CPU-runnable workload), on the GPU
-    for t in (1, 4, 16, 64, 256):
-        nbytes = rms_bytes(t, 1024, 4)
-        calls = []
-        for _ in range(sets_for(nbytes)):
-            x = torch.randn(t, 1024, device="cuda", generator=g)
-            w = 1.0 + 0.1 * torch.randn(1024, device="cuda", generator=g)
-            y = torch.empty_like(x)
-            calls.append(lambda x=x, w=w, y=y: ops.rms_norm_out(x, w, y, EPS))
-        record(f"rms_norm fp32 {t}x1024", calls, nbytes)
-
-    # Qwen3 decode Q/K norm + RoPE + paged KV store (one cache per case,
-    # distinct slots and positions per buffer set)
-    def qk_case(name, b, hq, hk, blocks, contiguous):
-        nbytes = qk_kv_bytes(b, hq, hk, 2)
-        n_sets = sets_for(nbytes)
-        kc = torch.zeros(blocks, 16, hk, 128, device="cuda", dtype=bf)
-        vc = torch.zeros_like(kc)
-        qw = (1 + 0.1 * torch.randn(128, device="cuda", generator=g)).to(bf)
-        kw = (1 + 0.1 * torch.randn(128, device="cuda", generator=g)).to(bf)
-        all_slots = torch.randperm(blocks * 16, generator=cpu_g)[: b * n_sets].to(torch.int32)
-        calls = []
-        for i in range(n_sets):
-            q = torch.randn(b, hq, 128, device="cuda", generator=g).to(bf)
-            k = torch.randn(b, hk, 128, device="cuda", generator=g).to(bf)
-            v = torch.randn(b, hk, 128, device="cuda", generator=g).to(bf)
-            if contiguous:
-                pos = torch.arange(b, device="cuda")
-                slots = torch.arange(b, device="cuda", dtype=torch.int32)
-            else:
-                pos = torch.randperm(32768, generator=cpu_g)[:b].cuda()
-                slots = all_slots[i * b:(i + 1) * b].cuda()
-            calls.append(lambda q=q, k=k, v=v, pos=pos, slots=slots: ops.fused_qk_rms_norm_rope_kv(
-                q, k, v, qw, kw, pos, cache, kc, vc, slots, EPS))
-        record(name, calls, nbytes)
-
-    qk_case("qk_kv decode bf16 B=1 16/8", 1, 16, 8, 2048, False)
-    for b in (64, 256, 1024):
-        qk_case(f"qk_kv decode bf16 B={b} 32/8", b, 32, 8, 65536, False)
-    qk_case("qk_kv prefill bf16 32768 tokens 64/8", 32768, 64, 8, 2048, True)
-
-    # prefill residual add + RMSNorm (4.3 GB per call: one call per graph)
-    x = torch.randn(65536, 8192, device="cuda", generator=g).to(bf)
-    r = torch.randn(65536, 8192, device="cuda", generator=g).to(bf)
-    w = (1 + 0.1 * torch.randn(8192, device="cuda", generator=g)).to(bf)
-    record("fused_add_rms_norm_inplace prefill bf16 65536x8192",
-           [lambda: ops.fused_add_rms_norm_inplace(x, r, w, EPS)], fused_bytes(65536, 8192, 2))
-    del x, r
-    return out
-
-
-def qk_cache_bytes(t: int, hq: int, hk: int, s: int, d: int = 128, rotary: int = 128,
-                   cache_elem: int | None = None) -> int:
-    # as qk_kv_bytes, with the two cache stores at the cache element size
-    cache_elem = s if cache_elem is None else cache_elem
-    return (t * (s * d * (2 * hq + 3 * hk) + 2 * cache_elem * d * hk + 8 + 4 + 4 * rotary)
-            + 2 * d * s)
-
-
-def norm_quant_bytes(t: int, h: int, s: int, add: bool, dynamic: bool) -> int:
-    # x read (and r read + written), fp8 result written, weight once, scales
-    return t * h * s * (3 if add else 1) + t * h + h * s + (4 * t if dynamic else 0)
+    def fused_qk_rms_norm_rope_kv(self, q, k, v, qw, kw, pos, cache, kc, vc, slots, eps=EPS,
+                                  version=1):
+        self.m.fused_qk_rms_norm_rope_kv(q, k, v, qw, kw, pos, cache, kc, vc, slots, eps, version)
 
 
 def vllm_ops():
@@ -593,6 +470,447 @@ def flashinfer_fused_add_rmsnorm():
         return norm.fused_add_rmsnorm
     except Exception:  # noqa: BLE001 - optional comparator
         return None
+
+
+def torch_native_fused(x, r, w):
+    """The reference benchmark's PyTorch-native arm: ``x + r`` then
+    ``F.rms_norm`` (out of place, two kernels)."""
+    import torch.nn.functional as F
+    summed = x + r
+    return F.rms_norm(summed, (x.shape[-1],), w, EPS), summed
+
+
+_COMPILED = {}
+
+
+def compiled(fn):
+    """torch.compile of a comparator function (fullgraph, static shapes), once
+    per function."""
+    if fn not in _COMPILED:
+        _COMPILED[fn] = torch.compile(fn, fullgraph=True, dynamic=False)
+    return _COMPILED[fn]
+
+
+def qk_reference_math(q, k, qw, kw, pos, cache):
+    from sm120_rmsnorm.reference import qk_rms_norm_rope_reference
+    return qk_rms_norm_rope_reference(q, k, qw, kw, pos, cache, EPS)
+
+
+# ---------------------------------------------------------------------------
+# per-config table
+# ---------------------------------------------------------------------------
+class PerConfig:
+    """us/call, GB/s and fraction of the HBM peak for every workload
+    configuration, timed by the graph protocol (module docstring). Sharded
+    configurations give each rank its share of the tokens / rows (own KV cache,
+    rank-local slots); at N > 1 rank 0 also times the whole problem alone
+    (``t1_us``) so the line carries strong-scaling efficiency
+    t1 / (N * tN). Comparators run at N = 1 only."""
+
+    def __init__(self, ops, flush, dist, args, peak):
+        self.ops, self.flush, self.dist, self.args, self.peak = ops, flush, dist, args, peak
+        self.reps = max(3, args.reps)
+        self.out = {}
+        self.g = torch.Generator(device="cuda").manual_seed(99 + dist.rank)
+        self.cpu_g = torch.Generator().manual_seed(7 + dist.rank)
+        want_cmp = dist.world == 1 and not args.skip_comparators
+        self.cmp_on = want_cmp
+        self.ref = ReferenceKernels.load() if want_cmp else None
+        self.cache = rope_table(32768)
+
+    # -- helpers ---------------------------------------------------------------
+    def us(self, calls) -> float:
+        us, _ = time_calls(calls, self.flush, self.reps)
+        return us
+
+    def comparators(self, build: dict) -> dict:
+        """{name: us} for each comparator builder (name -> () -> calls);
+        failures are recorded as unavailable."""
+        out = {}
+        if not self.cmp_on:
+            return out
+        for name, make in build.items():
+            if make is None:
+                continue
+            try:
+                calls = make()
+                us, how = time_calls(calls, self.flush, self.reps)
+                out[name] = round(us, 2) if how == "graph" else [round(us, 2), how]
+                del calls
+            except Exception as e:  # noqa: BLE001 - comparators may be unavailable
+                out[name] = f"unavailable: {type(e).__name__}: {str(e)[:80]}"
+                torch.cuda.synchronize()
+        return out
+
+    def put(self, name, us_local, nbytes, sharded=False, t1=None, cmp=None, latency_floor=2.0):
+        d = self.dist
+        us = d.max(us_local)
+        gbs = nbytes / (us * 1e-6) / 1e9
+        per_gpu = gbs / (d.world if sharded else 1)
+        if not sharded:
+            gbs *= d.world  # replicated: every rank moves nbytes
+        e = {"us": round(us, 3), "gbs": round(gbs, 1), "frac": round(per_gpu / self.peak, 3)}
+        if nbytes / (self.peak * 1e3) < latency_floor:  # bytes take < ~2 us at peak
+            e["latency_bound"] = True
+        if sharded and d.world > 1:
+            e["sharded"] = f"1/{d.world} per GPU"
+            if t1 is not None:
+                e["t1_us"] = round(t1, 3)
+                e["strong_eff"] = round(t1 / (d.world * us), 3)
+        if cmp:
+            e["cmp_us"] = cmp
+        self.out[name] = e
+        return e
+
+    def whole_on_rank0(self, build) -> float | None:
+        """Rank 0 times the unsharded problem alone (others wait); None at N = 1."""
+        d = self.dist
+        if d.world == 1:
+            return None
+        d.barrier()
+        us = 0.0
+        if d.rank == 0:
+            calls = build(0, None)
+            us = self.us(calls)
+            del calls
+            torch.cuda.empty_cache()
+        d.barrier()
+        return d.max(us)
+
+    # -- configurations ----------------------------------------------------------
+    def rms_fp32(self):
+        """fp32 RMSNorm rows of 1024 (the reference's CPU-runnable workload)."""
+        g = self.g
+        for t in (1, 4, 16, 64, 256):
+            nbytes = rms_bytes(t, 1024, 4)
+            sets = []
+            for _ in range(sets_for(nbytes)):
+                x = torch.randn(t, 1024, device="cuda", generator=g)
+                w = 1.0 + 0.1 * torch.randn(1024, device="cuda", generator=g)
+                sets.append((x, w, torch.empty_like(x)))
+            calls = [lambda s=s: self.ops.rms_norm_out(s[0], s[1], s[2], EPS) for s in sets]
+            cmp = self.comparators({
+                "reference_kernels": self.ref and (lambda: [
+                    lambda s=s: self.ref.rms_norm_out(s[0], s[1], s[2], EPS, 2) for s in sets])})
+            self.put(f"rms_norm fp32 {t}x1024", self.us(calls), nbytes, cmp=cmp)
+
+    def sweep(self):
+        """The fused add + RMSNorm sweep: step time of the 48 calls as one graph
+        and each shape's per-call time (replicated on every rank)."""
+        g = self.g
+        items = []
+        for t, h, name in sweep_shapes():
+            dt = DTYPES[name]
+            x = torch.randn(t, h, device="cuda", generator=g).to(dt)
+            r = torch.randn(t, h, device="cuda", generator=g).to(dt)
+            w = (1.0 + 0.1 * torch.randn(h, device="cuda", generator=g)).to(dt)
+            items.append((t, h, name, x, r, w))
+        step_bytes = sum(fused_bytes(t, h, 2) for t, h, *_ in items)
+
+        def step(ops):
+            return [lambda: [ops.fused_add_rms_norm_inplace(x, r, w, EPS)
+                             for *_, x, r, w in items]]
+
+        step_us = self.us(step(self.ops))
+        cmp = self.comparators({"reference_kernels": self.ref and (lambda: step(self.ref))})
+        e = self.put("fused_add sweep 48 calls (step)", step_us, step_bytes, cmp=cmp)
+        shapes = {}
+        for t, h, name, x, r, w in items:
+            nbytes = fused_bytes(t, h, 2)
+            bufs = [(x, r)] + [(torch.randn(t, h, device="cuda", generator=g).to(x.dtype),
+                                torch.randn(t, h, device="cuda", generator=g).to(x.dtype))
+                               for _ in range(sets_for(nbytes) - 1)]
+            us = self.dist.max(self.us([lambda bx=bx, br=br, w=w: self.ops.fused_add_rms_norm_inplace(
+                bx, br, w, EPS) for bx, br in bufs]))
+            shapes[f"{name} {t}x{h}"] = [round(us, 2), round(nbytes / (us * 1e-6) / 1e9, 1)]
+            del bufs
+        e["per_shape_us_gbs"] = shapes
+        return items
+
+    def fused_add_comparators(self, t, h):
+        """The headline op at one shape beside the reference's kernels, PyTorch
+        native (x + r; F.rms_norm), its torch.compile, FlashInfer and vLLM."""
+        g = self.g
+        nbytes = fused_bytes(t, h, 2)
+        w = (1 + 0.1 * torch.randn(h, device="cuda", generator=g)).to(torch.bfloat16)
+        sets = [(torch.randn(t, h, device="cuda", generator=g).to(torch.bfloat16),
+                 torch.randn(t, h, device="cuda", generator=g).to(torch.bfloat16))
+                for _ in range(sets_for(nbytes))]
+        ours = self.us([lambda x=x, r=r: self.ops.fused_add_rms_norm_inplace(x, r, w, EPS)
+                        for x, r in sets])
+        vllm = vllm_ops()
+        fi = flashinfer_fused_add_rmsnorm()
+        native_c = compiled(torch_native_fused)
+        cmp = self.comparators({
+            "reference_kernels": self.ref and (lambda: [
+                lambda x=x, r=r: self.ref.fused_add_rms_norm_inplace(x, r, w) for x, r in sets]),
+            "torch_native": lambda: [lambda x=x, r=r: torch_native_fused(x, r, w) for x, r in sets],
+            "torch_compile": lambda: [lambda x=x, r=r: native_c(x, r, w) for x, r in sets],
+            "flashinfer": fi and (lambda: [lambda x=x, r=r: fi(x, r, w, EPS) for x, r in sets]),
+            "vllm": vllm and (lambda: [lambda x=x, r=r: vllm[0].fused_add_rms_norm(x, r, w, EPS)
+                                       for x, r in sets]),
+        })
+        del sets
+        return ours, nbytes, cmp
+
+    def qk_kv(self, name, b_total, hq, hk, blocks, contiguous, sharded):
+        """Q/K norm + RoPE + paged KV store; sharded over sequences (tokens)."""
+        d = self.dist
+
+        def build(start, stop, ops=None):
+            ops = ops or self.ops
+            if stop is None:
+                start, stop = 0, b_total
+            b = stop - start
+            nbytes = qk_kv_bytes(b, hq, hk, 2)
+            n_sets = sets_for(nbytes)
+            bf = torch.bfloat16
+            kc = torch.zeros(blocks, 16, hk, 128, device="cuda", dtype=bf)
+            vc = torch.zeros_like(kc)
+            qw = (1 + 0.1 * torch.randn(128, device="cuda", generator=self.g)).to(bf)
+            kw = (1 + 0.1 * torch.randn(128, device="cuda", generator=self.g)).to(bf)
+            all_slots = torch.randperm(blocks * 16, generator=self.cpu_g)[: b * n_sets]
+            calls = []
+            for i in range(n_sets):
+                q = torch.randn(b, hq, 128, device="cuda", generator=self.g).to(bf)
+                k = torch.randn(b, hk, 128, device="cuda", generator=self.g).to(bf)
+                v = torch.randn(b, hk, 128, device="cuda", generator=self.g).to(bf)
+                if contiguous:  # prefill: positions of this shard, rank-local contiguous slots
+                    pos = torch.arange(start, stop, device="cuda")
+                    slots = torch.arange(b, device="cuda", dtype=torch.int32)
+                else:  # decode: distinct random positions, unique random slots
+                    pos = torch.randperm(32768, generator=self.cpu_g)[:b].cuda()
+                    slots = all_slots[i * b:(i + 1) * b].to(torch.int32).cuda()
+                calls.append(lambda q=q, k=k, v=v, pos=pos, slots=slots:
+                             ops.fused_qk_rms_norm_rope_kv(q, k, v, qw, kw, pos, self.cache, kc,
+                                                           vc, slots, EPS))
+            return calls
+
+        if sharded:
+            start, stop = shard_bounds(b_total, d.world, d.rank)
+        else:
+            start, stop = 0, b_total
+        calls = build(start, stop)
+        us = self.us(calls)
+        del calls
+        torch.cuda.empty_cache()
+        t1 = self.whole_on_rank0(lambda s, e: build(s, e)) if sharded else None
+        cmp = self.comparators({"reference_kernels": self.ref and (
+            lambda: build(0, b_total, self.ref))})
+        torch.cuda.empty_cache()
+        nbytes = qk_kv_bytes(b_total, hq, hk, 2)
+        return self.put(name, us, nbytes, sharded=sharded, t1=t1, cmp=cmp)
+
+    def qk_no_kv(self):
+        """Q/K norm + RoPE without the KV store (16 / 8 heads, positions
+        0..T-1), beside the reference's kernel and the eager / compiled
+        PyTorch statement of the math, as the reference's own benchmark
+        times it."""
+        bf = torch.bfloat16
+        compiled_math = compiled(qk_reference_math)
+        for t in (1, 4, 16, 64, 256):
+            nbytes = qk_bytes(t, 16, 8, 2)
+            qw = (1 + 0.1 * torch.randn(128, device="cuda", generator=self.g)).to(bf)
+            kw = (1 + 0.1 * torch.randn(128, device="cuda", generator=self.g)).to(bf)
+            pos = torch.arange(t, device="cuda")
+            sets = [(torch.randn(t, 16, 128, device="cuda", generator=self.g).to(bf),
+                     torch.randn(t, 8, 128, device="cuda", generator=self.g).to(bf))
+                    for _ in range(sets_for(nbytes))]
+            us = self.us([lambda q=q, k=k: self.ops.fused_qk_rms_norm_rope(
+                q, k, qw, kw, pos, self.cache, EPS) for q, k in sets])
+            cmp = self.comparators({
+                "reference_kernels": self.ref and (lambda: [
+                    lambda q=q, k=k: self.ref.fused_qk_rms_norm_rope(q, k, qw, kw, pos, self.cache)
+                    for q, k in sets]),
+                "torch_eager": lambda: [lambda q=q, k=k: qk_reference_math(
+                    q, k, qw, kw, pos, self.cache) for q, k in sets],
+                "torch_compile": lambda: [lambda q=q, k=k: compiled_math(
+                    q, k, qw, kw, pos, self.cache) for q, k in sets],
+            })
+            self.put(f"qk (no kv) bf16 T={t} 16/8", us, nbytes, cmp=cmp)
+            del sets
+
+    def run(self, headline_us: float, headline_t1):
+        d = self.dist
+        self.rms_fp32()
+        self.sweep()
+        if self.cmp_on:
+            us, nbytes, cmp = self.fused_add_comparators(1024, 4096)
+            self.put("fused_add bf16 1024x4096 (dominant sweep call)", us, nbytes, cmp=cmp)
+        self.qk_kv("qk_kv decode bf16 B=1 16/8", 1, 16, 8, 2048, False, sharded=False)
+        for b in (64, 256, 1024):
+            self.qk_kv(f"qk_kv decode bf16 B={b} 32/8", b, 32, 8, 65536, False, sharded=True)
+        self.qk_kv("qk_kv prefill bf16 32768 tokens 64/8", 32768, 64, 8, 2048, True,
+                   sharded=True)
+        self.qk_no_kv()
+        cmp = None
+        if self.cmp_on:
+            _, _, cmp = self.fused_add_comparators(HEADLINE_ROWS, HEADLINE_HIDDEN)
+        self.put("fused_add prefill bf16 65536x8192 (headline)", headline_us,
+                 fused_bytes(HEADLINE_ROWS, HEADLINE_HIDDEN, 2), sharded=True, t1=headline_t1,
+                 cmp=cmp)
+        return self.out
+
+
+# ---------------------------------------------------------------------------
+# GPU arm
+# ---------------------------------------------------------------------------
+def repeat_child(args) -> None:
+    """One process of the repeat protocol: the headline on one GPU,
+    REPEAT_SAMPLES samples of `steps` timed steps each; prints the samples."""
+    import sm120_rmsnorm as ops
+
+    torch.cuda.set_device(0)
+    head = PrefillRows(HEADLINE_ROWS, seed=1234)
+    samples = [headline_step_ms(ops, head, args.steps, args.warmup, _solo())
+               for _ in range(REPEAT_SAMPLES)]
+    print(json.dumps({"samples_ms": samples}))
+
+
+def spawn_repeats(extra_args: list[str], timeout: float) -> list[dict]:
+    """Run REPEAT_PROCESSES independent child processes of this script and
+    collect their JSON lines (the reference's run_repeated.py protocol)."""
+    env = {k: v for k, v in os.environ.items()
+           if k not in ("RANK", "LOCAL_RANK", "WORLD_SIZE", "LOCAL_WORLD_SIZE", "GROUP_RANK",
+                        "ROLE_RANK", "TORCHELASTIC_RUN_ID", "MASTER_ADDR", "MASTER_PORT")}
+    results = []
+    for _ in range(REPEAT_PROCESSES):
+        proc = subprocess.run([sys.executable, str(Path(__file__).resolve()), *extra_args],
+                              capture_output=True, text=True, env=env, timeout=timeout)
+        if proc.returncode != 0:
+            raise RuntimeError(f"repeat process failed (rc {proc.returncode}): "
+                               f"{(proc.stderr or proc.stdout)[-400:]}")
+        results.append(json.loads(proc.stdout.strip().splitlines()[-1]))
+    return results
+
+
+def repeat_summary(values: list[float], unit: str) -> dict:
+    med = statistics.median(values)
+    return {"processes": len(values), "median": round(med, 3), "unit": unit,
+            "range_pct": round(100.0 * (max(values) - min(values)) / med, 2),
+            "per_process": [round(v, 3) for v in values]}
+
+
+def gpu_arm(args, dist: "Dist") -> dict:
+    import sm120_rmsnorm as ops
+
+    peak, peak_source = measured_hbm_peak()
+    start, stop = shard_bounds(HEADLINE_ROWS, dist.world, dist.rank)
+    head = PrefillRows(stop - start, seed=1234 + dist.rank)
+    clocks = ClockSampler(sampled_gpus(dist.world) if dist.rank == 0 else None)
+    with clocks:
+        step_ms = headline_step_ms(ops, head, args.steps, args.warmup, dist)
+        step_ms_max = dist.max(step_ms)
+        if args.step_only:  # the timed steps alone (for a launch-list capture)
+            return {"metric": "step only", "ms_per_step": round(step_ms_max, 5),
+                    "gpu_launches": args.steps}
+        line = _measure_rest(args, dist, ops, head, step_ms_max, peak, peak_source)
+    line["clocks"] = clocks.summary() if dist.rank == 0 else None
+    # `roofline` (with the per-config table) last, so a truncated tail keeps it
+    line["roofline"] = line.pop("roofline")
+    return line
+
+
+def _measure_rest(args, dist, ops, head, step_ms_max, peak, peak_source) -> dict:
+    total_bytes = fused_bytes(HEADLINE_ROWS, HEADLINE_HIDDEN, 2)
+    value = total_bytes / (step_ms_max * 1e-3) / 1e9
+    launch_us = step_ms_max * 1e3  # one launch per step on each rank
+    achieved = head.bytes / (launch_us * 1e-6) / 1e9
+    roofline = {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
+                "frac": round(achieved / peak, 4), "traffic": dram_traffic_per_launch(head.rows),
+                "kernel": f"fused_add_rms_norm_inplace bf16 {head.rows}x{HEADLINE_HIDDEN} "
+                          "(one launch per step on each GPU; the slowest rank's)",
+                "timing": "CUDA events around the timed steps on the launching stream; "
+                          "launch duration = step time",
+                "algorithmic_bytes_per_launch": head.bytes, "launch_us": round(launch_us, 2),
+                "traffic_source": "ncu dram__bytes_read.sum + dram__bytes_write.sum of a "
+                                  "smaller launch of the same kernel, scaled by rows "
+                                  "(profiles/dram_traffic.txt)",
+                "peak_source": peak_source + (", of measured" if peak_source.startswith("measured")
+                                              else ", of fallback")}
+
+    e2e = e2e_headline(ops, head, args.steps, dist)
+
+    # whole problem on one GPU, for the headline's strong-scaling entry
+    headline_t1 = None
+    if dist.world > 1:
+        dist.barrier()
+        t1 = 0.0
+        if dist.rank == 0:
+            whole = PrefillRows(HEADLINE_ROWS, seed=1234)
+            t1 = headline_step_ms(ops, whole, args.steps, args.warmup, _solo()) * 1e3
+            del whole
+            torch.cuda.empty_cache()
+        dist.barrier()
+        headline_t1 = dist.max(t1)
+
+    flush = Flusher()
+    per_config = {} if args.skip_per_config else PerConfig(ops, flush, dist, args, peak).run(
+        launch_us, headline_t1)
+    del flush
+    torch.cuda.empty_cache()
+
+    if dist.world == 1 and not args.skip_repeat:
+        runs = spawn_repeats(["--repeat-child", "--steps", str(args.steps),
+                              "--warmup", str(args.warmup)], timeout=600)
+        per_process = [statistics.median(r["samples_ms"]) for r in runs]
+        rep = repeat_summary([total_bytes / (ms * 1e-3) / 1e9 for ms in per_process], "GB/s")
+        rep["ms_per_step_per_process"] = [round(ms, 4) for ms in per_process]
+        rep["protocol"] = (f"{REPEAT_PROCESSES} independent processes x {REPEAT_SAMPLES} samples "
+                           f"of {args.steps} timed steps (after {args.warmup} warm-up steps); "
+                           "median of the per-process medians")
+        roofline["repeat"] = rep
+    roofline["per_config"] = per_config
+
+    if args.detail:
+        detail = {}
+        flush = Flusher()
+        detail["extensions"] = extension_suite(flush, dist, args)
+        detail["engine"] = engine_suite(flush, dist, args)
+        detail["projection"] = projection_suite(flush, dist, args)
+        del flush
+        if dist.rank == 0:
+            Path(args.detail).parent.mkdir(parents=True, exist_ok=True)
+            Path(args.detail).write_text(json.dumps(detail, indent=1))
+
+    return {
+        "metric": METRIC, "value": round(value, 2), "unit": "GB/s", "n_gpus": dist.world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(step_ms_max, 5),
+        "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "bf16",
+        "data": "synthetic (seeded N(0,1) activations, N(1,0.1) weights)",
+        "gpu_launches": args.steps,
+        "config": {"workload": HEADLINE_WORKLOAD, "rows": HEADLINE_ROWS,
+                   "hidden": HEADLINE_HIDDEN, "rows_per_gpu": head.rows,
+                   "bytes_per_step": total_bytes,
+                   "parallelism": f"rows sharded over {dist.world} GPU(s), no collective on the "
+                                  "data path (NCCL only for barriers and the max-over-ranks time)",
+                   "l2": "not flushed: each rank's x + residual (2 GiB / N) exceeds L2; the "
+                         "per-config table flushes L2 (512 MiB write) before every timing"},
+        "e2e": e2e, "roofline": roofline, "device": torch.cuda.get_device_name(),
+    }
+
+
+def _solo() -> "Dist":
+    solo = Dist.__new__(Dist)
+    solo.world, solo.rank, solo.local_rank, solo.pg = 1, 0, 0, None
+    return solo
+
+
+# ---------------------------------------------------------------------------
+# detail suites (--detail): the engine-side extensions, the engine step and the
+# QKV projection beside library comparators
+# ---------------------------------------------------------------------------
+def qk_cache_bytes(t: int, hq: int, hk: int, s: int, d: int = 128, rotary: int = 128,
+                   cache_elem: int | None = None) -> int:
+    # as qk_kv_bytes, with the two cache stores at the cache element size
+    cache_elem = s if cache_elem is None else cache_elem
+    return (t * (s * d * (2 * hq + 3 * hk) + 2 * cache_elem * d * hk + 8 + 4 + 4 * rotary)
+            + 2 * d * s)
+
+
+def norm_quant_bytes(t: int, h: int, s: int, add: bool, dynamic: bool) -> int:
+    # x read (and r read + written), fp8 result written, weight once, scales
+    return t * h * s * (3 if add else 1) + t * h + h * s + (4 * t if dynamic else 0)
 
 
 def extension_suite(flush: Flusher, dist: Dist, args) -> dict:
@@ -982,81 +1300,83 @@ def host_threads() -> int:
         return os.cpu_count() or 1
 
 
-def cpu_sweep_gbs(seconds: float, threads: int, passes: int | None = None):
+def cpu_rows(rows: int, seed: int):
+    """x, residual [rows, 8192] bf16 and the weight on the host, drawn from
+    N(0,1) / N(1,0.1): one seeded 2048-row block repeated down the rows (the
+    CPU's caches hold far less than a block, so the timing is that of the
+    full-size arrays; drawing 2^29 normals would take longer than the timing)."""
+    g = torch.Generator().manual_seed(seed)
+    block = min(rows, 2048)
+    h = HEADLINE_HIDDEN
+    xb = torch.randn(block, h, generator=g).to(torch.bfloat16)
+    rb = torch.randn(block, h, generator=g).to(torch.bfloat16)
+    w = (1 + 0.1 * torch.randn(h, generator=g)).to(torch.bfloat16)
+    reps = (rows + block - 1) // block
+    x = xb.repeat(reps, 1)[:rows].contiguous()
+    r = rb.repeat(reps, 1)[:rows].contiguous()
+    return x, r, w
+
+
+def cpu_port_timing(rows: int, threads: int, calls: int | None, seconds: float,
+                    warmup: int = 1):
+    """The C restatement of the reference's CPU path, in place on [rows, 8192]
+    bf16 host arrays: `warmup` untimed calls, then `calls` timed calls (or as
+    many as fit in `seconds`). Returns (GB/s, calls, elapsed s, per-call s)."""
     from oracle import oracle
 
     oracle.build()
     oracle.set_threads(threads)
-    g = torch.Generator().manual_seed(4321)
-    items = []
-    for t, h, name in sweep_shapes():
-        dt = DTYPES[name]
-        x = torch.randn(t, h, generator=g).to(dt)
-        r = torch.randn(t, h, generator=g).to(dt)
-        w = (1 + 0.1 * torch.randn(h, generator=g)).to(dt)
-        items.append((x, r, w))
-    total = sum(fused_bytes(x.shape[0], x.shape[1], x.element_size()) for x, _, _ in items)
-    for x, r, w in items:  # warm-up pass
+    x, r, w = cpu_rows(rows, seed=4321)
+    nbytes = fused_bytes(rows, HEADLINE_HIDDEN, 2)
+    for _ in range(warmup):
         oracle.fused_add_rms_norm_out(x, r, w, x, r, EPS)
-    done, t0 = 0, time.perf_counter()
+    per_call = []
+    t0 = time.perf_counter()
     while True:
-        for x, r, w in items:
-            oracle.fused_add_rms_norm_out(x, r, w, x, r, EPS)
-        done += 1
+        c0 = time.perf_counter()
+        oracle.fused_add_rms_norm_out(x, r, w, x, r, EPS)
+        per_call.append(time.perf_counter() - c0)
         elapsed = time.perf_counter() - t0
-        if (passes is not None and done >= passes) or (passes is None and elapsed >= seconds):
+        if (calls is not None and len(per_call) >= calls) or (calls is None and elapsed >= seconds):
             break
-    return total * done / elapsed / 1e9, done, elapsed
+    return nbytes * len(per_call) / elapsed / 1e9, len(per_call), elapsed, per_call
 
 
-class ReferenceKernels:
-    """The reference project's own CUDA kernels (compiled for sm_100a from its
-    sources by oracle/build_ref.py), called with its ops.py default versions."""
-
-    def __init__(self, module):
-        self.m = module
-
-    def fused_add_rms_norm_inplace(self, x, r, w, eps=EPS, version=0):
-        self.m.fused_add_rms_norm_inplace(x, r, w, eps, version)
-
-    def rms_norm_out(self, x, w, out, eps=EPS, version=2):
-        self.m.rms_norm_out(x, w, out, eps, version)
-
-    def fused_qk_rms_norm_rope_kv(self, q, k, v, qw, kw, pos, cache, kc, vc, slots, eps=EPS,
-                                  version=1):
-        self.m.fused_qk_rms_norm_rope_kv(q, k, v, qw, kw, pos, cache, kc, vc, slots, eps, version)
+def reference_child(args) -> None:
+    """One process of the reference arm: the headline workload through the C
+    restatement of the reference's CPU path on all host threads."""
+    threads = host_threads()
+    gbs, calls, elapsed, per_call = cpu_port_timing(HEADLINE_ROWS, threads, args.steps, 0,
+                                                    warmup=args.warmup)
+    print(json.dumps({"gbs": gbs, "calls": calls, "elapsed_s": elapsed,
+                      "ms_per_step": elapsed / calls * 1e3, "threads": threads}))
 
 
-def reference_kernels_gpu(args, dist: Dist) -> dict:
-    """The reference's CUDA kernels on this B200, same workload and timing as
-    the main arm (the SM120 kernels rebuilt for sm_100a: the bar to beat)."""
+def reference_kernels_gpu(args) -> dict:
+    """The reference's CUDA kernels on this B200 on the headline workload
+    (the SM120 kernels rebuilt for sm_100a: the bar to beat), same steps and
+    warm-up as the GPU arm."""
     if not torch.cuda.is_available():
         return {"unavailable": "no CUDA device"}
-    from oracle import build_ref
-
-    module = build_ref.load()
-    if module is None:
+    ref = ReferenceKernels.load()
+    if ref is None:
         return {"unavailable": "the reference's kernels were not built (oracle/build_ref.py "
                                "needs the reference checkout)"}
     torch.cuda.set_device(0)
-    ops = ReferenceKernels(module)
-    flush = Flusher()
-    data = SweepData(seed=1234)
-    step_ms = sweep_step_ms(ops, data, flush, args.steps, args.warmup, dist)
-    per_shape = per_shape_times(ops, data, flush, dist, args)
-    per_op = {} if args.skip_per_op else per_op_suite(ops, flush, dist, args)
-    return {"value": round(data.bytes / (step_ms * 1e-3) / 1e9, 2), "unit": "GB/s",
-            "ms_per_step": round(step_ms, 5),
+    head = PrefillRows(HEADLINE_ROWS, seed=1234)
+    ms = headline_step_ms(ref, head, args.steps, args.warmup, _solo())
+    return {"value": round(head.bytes / (ms * 1e-3) / 1e9, 2), "unit": "GB/s",
+            "ms_per_step": round(ms, 4), "steps": args.steps, "warmup": args.warmup,
             "build": "reference csrc/rmsnorm_kernels.cu + bindings.cpp, nvcc -O3 "
                      "--use_fast_math -gencode arch=compute_100a,code=sm_100a",
-            "per_shape": per_shape, "per_op": per_op}
+            "call": "fused_add_rms_norm_inplace(x, residual, weight, 1e-6, version=0)"}
 
 
-def pytorch_cpu_reference_gbs(steps: int, threads: int) -> dict:
+def pytorch_cpu_reference(threads: int, rows: int = 2048, calls: int = 5) -> dict:
     """The reference's PyTorch oracle math (residual add + RMSNorm,
     reference.py:14-24 in the reference project; restated op for op in
-    sm120_rmsnorm/reference.py, loaded here by file path so nothing else of
-    the package is imported) on the host CPU over the sweep."""
+    sm120_rmsnorm/reference.py, loaded by file path so nothing else of the
+    package is imported) on the host CPU, on a bounded sample of the rows."""
     import importlib.util
 
     path = ROOT / "sm120-norm-fusion-kernels_b200" / "sm120_rmsnorm" / "reference.py"
@@ -1064,56 +1384,49 @@ def pytorch_cpu_reference_gbs(steps: int, threads: int) -> dict:
     module = importlib.util.module_from_spec(spec)
     spec.loader.exec_module(module)
     torch.set_num_threads(threads)
-    g = torch.Generator().manual_seed(4321)
-    items = []
-    for t, h, name in sweep_shapes():
-        dt = DTYPES[name]
-        items.append((torch.randn(t, h, generator=g).to(dt), torch.randn(t, h, generator=g).to(dt),
-                      (1 + 0.1 * torch.randn(h, generator=g)).to(dt)))
-    total = sum(fused_bytes(x.shape[0], x.shape[1], x.element_size()) for x, _, _ in items)
-    for x, r, w in items:
-        module.fused_add_rms_norm_reference(x, r, w, EPS)
+    x, r, w = cpu_rows(rows, seed=4321)
+    module.fused_add_rms_norm_reference(x, r, w, EPS)
     t0 = time.perf_counter()
-    for _ in range(steps):
-        for x, r, w in items:
-            module.fused_add_rms_norm_reference(x, r, w, EPS)
+    for _ in range(calls):
+        module.fused_add_rms_norm_reference(x, r, w, EPS)
     elapsed = time.perf_counter() - t0
-    return {"value": round(total * steps / elapsed / 1e9, 3), "unit": "GB/s", "threads": threads,
-            "sample": f"{steps} passes over the 48-call sweep, {elapsed:.2f} s"}
+    return {"value": round(fused_bytes(rows, HEADLINE_HIDDEN, 2) * calls / elapsed / 1e9, 3),
+            "unit": "GB/s", "threads": threads,
+            "sample": f"{calls} calls on {rows} of the 65536 rows, {elapsed:.2f} s"}
 
 
-def reference_arm(args, dist: Dist) -> dict:
+def reference_arm(args) -> dict:
     """The reference path's CPU implementation (C restatement of its PyTorch
-    oracle) on the host cores, on the same sweep; rank 0 only."""
-    threads = host_threads()
-    from oracle import oracle
-
-    oracle.build()
-    oracle.set_threads(threads)
-    for _ in range(args.warmup):
-        cpu_sweep_gbs(0, threads, passes=1)
-    gbs, passes, elapsed = cpu_sweep_gbs(0, threads, passes=args.steps)
-    sample = (f"{passes} passes over the 48-call sweep (one step each), "
-              f"{elapsed:.2f} s of CPU time")
+    oracle) on the host cores, on the headline workload, in REPEAT_PROCESSES
+    independent processes of `steps` timed calls each; rank 0 only."""
+    runs = spawn_repeats(["--impl", "reference", "--reference-child", "--steps",
+                          str(args.steps), "--warmup", str(args.warmup)], timeout=900)
+    values = [r["gbs"] for r in runs]
+    rep = repeat_summary(values, "GB/s")
+    value = rep["median"]
+    ms = statistics.median(r["ms_per_step"] for r in runs)
+    threads = runs[0]["threads"]
+    timed = sum(r["elapsed_s"] for r in runs)
+    sample = (f"the full workload, {args.steps} timed calls (after {args.warmup} warm-up calls) "
+              f"in each of {REPEAT_PROCESSES} processes, {timed:.1f} s timed in all; median of "
+              "the per-process GB/s")
+    rep["protocol"] = sample
     return {
-        "impl": "reference",
-        "metric": "achieved HBM GB/s (% of B200 peak) and us/call per op at 1/2/4/8 GPUs",
-        "value": round(gbs, 3), "unit": "GB/s", "n_gpus": dist.world, "steps": args.steps,
-        "warmup": args.warmup, "ms_per_step": round(elapsed / passes * 1e3, 3),
-        "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
-        "dtype": "bf16+fp16 (fp32 accumulate)", "data": "synthetic",
-        "config": {"workload": "in-place residual add + RMSNorm sweep: tokens "
-                               "{1,4,16,64,256,1024} x hidden {768,1024,2048,4096} x "
-                               "{bf16,fp16}", "parallelism": "host cores"},
-        "cpu_baseline": {"value": round(gbs, 3), "unit": "GB/s", "cores": threads,
-                         "kind": "port", "sample": sample},
-        "e2e": {"value": round(gbs, 3), "unit": "GB/s", "h2d_bytes_per_step": 0,
-                "d2h_bytes_per_step": 0},
+        "impl": "reference", "metric": METRIC, "value": value, "unit": "GB/s",
+        "n_gpus": int(os.environ.get("WORLD_SIZE", "1")), "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": round(ms, 3), "higher_is_better": True,
+        "scaling": "strong", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+        "config": {"workload": HEADLINE_WORKLOAD, "rows": HEADLINE_ROWS,
+                   "hidden": HEADLINE_HIDDEN, "parallelism": f"{threads} host threads (OpenMP)"},
+        "cpu_baseline": {"value": value, "unit": "GB/s", "cores": threads, "kind": "port",
+                         "sample": sample},
+        "e2e": {"value": value, "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+        "repeat": rep,
         "note": "the reference's CPU path is its PyTorch oracle (sm120_rmsnorm/reference.py), "
-                "which cannot travel; this is its C restatement (oracle/norm_oracle.c), "
-                "pinned to the reference's own outputs by the golden-vector tests",
-        "reference_pytorch_cpu": pytorch_cpu_reference_gbs(max(3, args.steps // 4), threads),
-        "reference_kernels_b200": reference_kernels_gpu(args, dist),
+                "which cannot travel; this is its C restatement (oracle/norm_oracle.c), pinned "
+                "to the reference's own outputs by the golden-vector tests",
+        "reference_pytorch_cpu": pytorch_cpu_reference(threads),
+        "reference_kernels_b200": reference_kernels_gpu(args),
     }
 
 
@@ -1217,15 +1530,21 @@ def profile_case(args) -> None:
 def main():
     parser = argparse.ArgumentParser(description=__doc__.splitlines()[0])
     parser.add_argument("--gpus", type=int, default=1)
-    parser.add_argument("--steps", type=int, default=50)
+    parser.add_argument("--steps", type=int, default=20)
     parser.add_argument("--warmup", type=int, default=5)
-    parser.add_argument("--reps", type=int, default=10, help="launches per per-kernel timing")
+    parser.add_argument("--reps", type=int, default=10, help="replays per per-config timing")
     parser.add_argument("--impl", choices=["b200", "reference"], default="b200")
     parser.add_argument("--cpu-seconds", type=float, default=10.0)
-    parser.add_argument("--skip-per-op", action="store_true")
+    parser.add_argument("--skip-per-config", action="store_true")
+    parser.add_argument("--skip-comparators", action="store_true")
     parser.add_argument("--skip-cpu", action="store_true")
+    parser.add_argument("--skip-repeat", action="store_true")
+    parser.add_argument("--detail", help="also run the extension / engine / projection suites "
+                                         "and write them to this JSON file")
     parser.add_argument("--step-only", action="store_true",
                         help="run warm-up and the timed steps only (launch-list captures)")
+    parser.add_argument("--repeat-child", action="store_true", help=argparse.SUPPRESS)
+    parser.add_argument("--reference-child", action="store_true", help=argparse.SUPPRESS)
     parser.add_argument("--profile", choices=["fused", "rms", "qkkv", "qk", "qkcache", "quant", "fp4",
                                               "projection"],
                         help="launch one operator at one shape and exit (ncu driver)")
@@ -1243,6 +1562,12 @@ def main():
         return
     if args.warmup < 3:
         parser.error("--warmup must be at least 3")
+    if args.repeat_child:
+        repeat_child(args)
+        return
+    if args.reference_child:
+        reference_child(args)
+        return
 
     dist = Dist()
     if args.gpus > 1 and dist.world == 1:
@@ -1258,7 +1583,7 @@ def main():
     if args.impl == "reference":
         if dist.rank != 0:
             return
-        print(json.dumps(reference_arm(args, dist)))
+        print(json.dumps(reference_arm(args)))
         return
 
     dist.init()
@@ -1266,11 +1591,14 @@ def main():
         line = gpu_arm(args, dist)
         if dist.rank == 0 and dist.world == 1 and not args.skip_cpu and not args.step_only:
             threads = host_threads()
-            gbs, passes, elapsed = cpu_sweep_gbs(args.cpu_seconds, threads)
+            gbs, calls, elapsed, _ = cpu_port_timing(HEADLINE_ROWS, threads, None,
+                                                     args.cpu_seconds)
             line["cpu_baseline"] = {
                 "value": round(gbs, 3), "unit": "GB/s", "cores": threads, "kind": "port",
-                "sample": f"{passes} passes over the 48-call sweep in {elapsed:.1f} s "
-                          f"(C restatement of the reference's PyTorch oracle, OpenMP)"}
+                "sample": f"{calls} in-place calls on the full [65536, 8192] bf16 x and residual "
+                          f"in {elapsed:.1f} s (C restatement of the reference's PyTorch oracle, "
+                          "OpenMP)"}
+            line["roofline"] = line.pop("roofline")
         if dist.rank == 0:
             print(json.dumps(line))
     finally:

@@ -24,7 +24,6 @@ from pathlib import Path
 HERE = Path(__file__).resolve().parent
 OUT = HERE / "_ref"
 MODULE = "sm120_reference_C"
-DEFAULT_REFERENCE = Path("/root/reference")
 CUDA_HOME = Path(os.environ.get("CUDA_HOME", "/usr/local/cuda"))
 
 
@@ -39,7 +38,15 @@ def _run(cmd):
         raise RuntimeError(f"reference build step failed: {cmd[0]}")
 
 
-def build(reference: Path = DEFAULT_REFERENCE, force: bool = False) -> Path:
+def reference_root(reference: Path | str | None = None) -> Path | None:
+    """The reference checkout to build from: `reference`, else the
+    SM120N_REFERENCE_ROOT environment variable; None when neither is given."""
+    if reference is None:
+        reference = os.environ.get("SM120N_REFERENCE_ROOT")
+    return Path(reference) if reference else None
+
+
+def build(reference: Path, force: bool = False) -> Path:
     import torch
     from torch.utils import cpp_extension
 
@@ -77,11 +84,13 @@ def build(reference: Path = DEFAULT_REFERENCE, force: bool = False) -> Path:
     return target
 
 
-def build_if_present(reference: Path = DEFAULT_REFERENCE) -> Path | None:
-    """Build when the reference checkout exists (this container); elsewhere use
-    whatever was built before, if anything."""
-    if (reference / "csrc" / "rmsnorm_kernels.cu").exists():
-        return build(reference)
+def build_if_present(reference: Path | str | None = None) -> Path | None:
+    """Build when a reference checkout is given (argument or
+    SM120N_REFERENCE_ROOT) and present; otherwise use whatever was built
+    before, if anything."""
+    root = reference_root(reference)
+    if root is not None and (root / "csrc" / "rmsnorm_kernels.cu").exists():
+        return build(root)
     return module_path() if module_path().exists() else None
 
 
@@ -96,4 +105,14 @@ def load():
 
 
 if __name__ == "__main__":
-    print(build(force="--force" in sys.argv))
+    import argparse
+
+    parser = argparse.ArgumentParser(description=__doc__.splitlines()[0])
+    parser.add_argument("--reference", type=Path, default=None,
+                        help="reference checkout (default: $SM120N_REFERENCE_ROOT)")
+    parser.add_argument("--force", action="store_true")
+    cli = parser.parse_args()
+    root = reference_root(cli.reference)
+    if root is None:
+        parser.error("give --reference or set SM120N_REFERENCE_ROOT")
+    print(build(root, force=cli.force))

@@ -13,6 +13,7 @@ entry naming the element type.
 from __future__ import annotations
 
 import argparse
+import os
 import importlib.util
 from pathlib import Path
 
@@ -62,8 +63,13 @@ def save(name: str, **arrays) -> None:
 
 def main() -> None:
     parser = argparse.ArgumentParser(description=__doc__.splitlines()[0])
-    parser.add_argument("--reference", type=Path, default=Path("/root/reference"))
+    parser.add_argument("--reference", type=Path, default=None,
+                        help="reference checkout (default: $SM120N_REFERENCE_ROOT)")
     args = parser.parse_args()
+    if args.reference is None:
+        if not os.environ.get("SM120N_REFERENCE_ROOT"):
+            parser.error("give --reference or set SM120N_REFERENCE_ROOT")
+        args.reference = Path(os.environ["SM120N_REFERENCE_ROOT"])
     ref = load_reference(args.reference)
     eps = 1e-6
 
