@@ -641,16 +641,25 @@ class PerConfig:
         vllm = vllm_ops()
         fi = flashinfer_fused_add_rmsnorm()
         native_c = compiled(torch_native_fused)
+        # out-of-place comparators keep every call's outputs alive, so each call
+        # writes its own fresh buffers (a freed output would be reused by the next
+        # call and its writes would stay in L2)
+        keep = [None] * len(sets)
+
+        def kept(fn):
+            return [lambda i=i, x=x, r=r: keep.__setitem__(i, fn(x, r, w))
+                    for i, (x, r) in enumerate(sets)]
+
         cmp = self.comparators({
             "reference_kernels": self.ref and (lambda: [
                 lambda x=x, r=r: self.ref.fused_add_rms_norm_inplace(x, r, w) for x, r in sets]),
-            "torch_native": lambda: [lambda x=x, r=r: torch_native_fused(x, r, w) for x, r in sets],
-            "torch_compile": lambda: [lambda x=x, r=r: native_c(x, r, w) for x, r in sets],
+            "torch_native": lambda: kept(torch_native_fused),
+            "torch_compile": lambda: kept(native_c),
             "flashinfer": fi and (lambda: [lambda x=x, r=r: fi(x, r, w, EPS) for x, r in sets]),
             "vllm": vllm and (lambda: [lambda x=x, r=r: vllm[0].fused_add_rms_norm(x, r, w, EPS)
                                        for x, r in sets]),
         })
-        del sets
+        del sets, keep
         return ours, nbytes, cmp
 
     def qk_kv(self, name, b_total, hq, hk, blocks, contiguous, sharded):
@@ -718,17 +727,21 @@ class PerConfig:
                     for _ in range(sets_for(nbytes))]
             us = self.us([lambda q=q, k=k: self.ops.fused_qk_rms_norm_rope(
                 q, k, qw, kw, pos, self.cache, EPS) for q, k in sets])
+            keep = [None] * len(sets)  # every call's outputs stay alive (fresh buffers)
+
+            def kept(fn):
+                return [lambda i=i, q=q, k=k: keep.__setitem__(i, fn(q, k, qw, kw, pos, self.cache))
+                        for i, (q, k) in enumerate(sets)]
+
             cmp = self.comparators({
                 "reference_kernels": self.ref and (lambda: [
                     lambda q=q, k=k: self.ref.fused_qk_rms_norm_rope(q, k, qw, kw, pos, self.cache)
                     for q, k in sets]),
-                "torch_eager": lambda: [lambda q=q, k=k: qk_reference_math(
-                    q, k, qw, kw, pos, self.cache) for q, k in sets],
-                "torch_compile": lambda: [lambda q=q, k=k: compiled_math(
-                    q, k, qw, kw, pos, self.cache) for q, k in sets],
+                "torch_eager": lambda: kept(qk_reference_math),
+                "torch_compile": lambda: kept(compiled_math),
             })
             self.put(f"qk (no kv) bf16 T={t} 16/8", us, nbytes, cmp=cmp)
-            del sets
+            del sets, keep
 
     def run(self, headline_us: float, headline_t1):
         d = self.dist

@@ -42,7 +42,7 @@
 extern "C" {
 #endif
 
-#define SM120N_ABI_VERSION 4
+#define SM120N_ABI_VERSION 5
 
 #if defined(__GNUC__)
 #define SM120N_API __attribute__((visibility("default")))
@@ -91,6 +91,20 @@ SM120N_API int sm120n_get_programmatic_launch(void);
  */
 SM120N_API int sm120n_get_device_faults(uint32_t* out_count);
 SM120N_API int sm120n_reset_device_faults(void);
+
+/*
+ * Diagnostic: the number of polls a kernel makes while waiting for its own
+ * bulk copies (the row kernels that stage rows in shared memory) to land
+ * before it gives up, records an expired wait in the fault counter and
+ * leaves its rows unwritten. 0 restores the default (2^22 polls, far
+ * beyond any real copy); values above it are clamped to it. Lowering it lets
+ * a test make the bound expire without faulting or hanging anything: the
+ * kernel still waits, with the full bound, for its copies to land before it
+ * exits. Process-wide; no reference counterpart (the reference has no
+ * asynchronous copies).
+ */
+SM120N_API void sm120n_set_wait_limit(uint32_t polls);
+SM120N_API uint32_t sm120n_get_wait_limit(void);
 
 /*
  * RMSNorm: output[i, :] = round(x[i, :] * (1 / sqrt(mean(x[i, :]^2) + eps)) * weight)

@@ -326,6 +326,34 @@ __device__ __forceinline__ bool mbarrier_wait_bounded(uint64_t* bar, uint32_t pa
   return false;
 }
 
+// Non-blocking test of the phase (no suspension, unlike try_wait).
+__device__ __forceinline__ bool mbarrier_test_wait(uint64_t* bar, uint32_t parity) {
+  uint32_t done;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.test_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(done)
+      : "r"(shared_address(bar)), "r"(parity)
+      : "memory");
+  return done != 0;
+}
+
+// A wait for copies to land with the caller's poll limit (the host passes the
+// process-wide limit, sm120n_set_wait_limit). At the default limit it is
+// mbarrier_wait_bounded; a lowered limit polls without suspending, so a
+// limit of a few polls gives up before any copy from memory can have landed
+// (a test of the expiry path). Callers that give up must still drain their
+// copies with mbarrier_wait_bounded before leaving.
+__device__ __forceinline__ bool mbarrier_wait_limited(uint64_t* bar, uint32_t parity,
+                                                      uint32_t polls) {
+  if (polls >= kMaxBarrierPolls) return mbarrier_wait_bounded(bar, parity);
+  for (uint32_t i = 0; i < polls; ++i) {
+    if (mbarrier_test_wait(bar, parity)) return true;
+  }
+  return false;
+}
+
 // Asks L2 for `bytes` (a multiple of 16) at 16-byte-aligned global `p`; no
 // data is returned and nothing waits for it. Kernels issue these for inputs
 // before waiting for the upstream grid (programmatic dependent launch): a

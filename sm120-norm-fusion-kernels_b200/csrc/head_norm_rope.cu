@@ -86,7 +86,11 @@ __global__ void __launch_bounds__(256, sizeof(T) == 2 ? (kHoistWeights ? 4 : 5) 
     // block's first two passes (threads 0-4 and 5-9) and their tokens'
     // position and slot (batch-1 decode: 1.86 us against 2.11 us; B = 1024,
     // where 540 of 740 blocks make a second pass: 7.36 against 7.87 us with
-    // the first pass alone).
+    // the first pass alone). Pass p of block b covers units
+    // [(b + p * gridDim.x) * per_block, +per_block) for every block size (the
+    // loop below walks warps in that order), so the request matches the
+    // block's own pass; a grid that covers all units in one pass (versions 1
+    // and 4, small calls) has no pass 1 and skips the request.
     const uint32_t heads = static_cast<uint32_t>(a.query_heads + a.key_heads);
     const uint32_t units = static_cast<uint32_t>(a.tokens) * heads;
     const uint32_t per_block = (blockDim.x / kWarpSize) * kHeadsPerWarp;

@@ -893,6 +893,7 @@ __global__ void __launch_bounds__(4 * kWarpSize, 2)
   __shared__ __align__(8) uint64_t done;
   __shared__ uint32_t tmem_slot;
   __shared__ int aborted;
+  __shared__ int cta_ok;  // this CTA's main loop completed; read by every CTA of the cluster
   unsigned char* tiles = reinterpret_cast<unsigned char*>(
       (reinterpret_cast<uintptr_t>(dynamic_smem) + 1023) & ~uintptr_t{1023});
   float* partial = reinterpret_cast<float*>(tiles);  // after the main loop
@@ -988,10 +989,19 @@ __global__ void __launch_bounds__(4 * kWarpSize, 2)
   }
 #pragma unroll
   for (int p = 0; p < kPasses; ++p) head_row_fetch_tables(job[p], a, n_tile, lane & 7);
-  cluster.sync();  // every CTA's partial tile is in place
+  const int ok = __syncthreads_and(ready && !aborted);
+  if (threadIdx.x == 0) cta_ok = ok;
+  cluster.sync();  // every CTA's partial tile and verdict are in place
+
+  // The rows are finished only if every CTA of the cluster completed its
+  // slice: a CTA whose wait expired wrote no partial tile (its expiry is in
+  // the fault counter), and its siblings must not sum what is in its place.
+  bool cluster_ok = true;
+#pragma unroll
+  for (int s = 0; s < kSplits; ++s) cluster_ok = cluster_ok && *cluster.map_shared_rank(&cta_ok, s);
 
   // sum the partials of this CTA's rows in rank order
-  for (int idx = threadIdx.x; idx < S::kRows * kHead / 4; idx += S::kThreads) {
+  for (int idx = threadIdx.x; cluster_ok && idx < S::kRows * kHead / 4; idx += S::kThreads) {
     const int r = idx / (kHead / 4);
     const int col = (idx - r * (kHead / 4)) * 4;
     const int offset = (rank * S::kRows + r) * kSplitRowFloats + col;
@@ -1006,7 +1016,7 @@ __global__ void __launch_bounds__(4 * kWarpSize, 2)
     reinterpret_cast<uint32_t*>(&rows[r][col])[1] = Pack<__nv_bfloat16>::f32_to_word(sum.z, sum.w);
   }
   __syncthreads();
-  if (ready && !aborted) {
+  if (cluster_ok) {
 #pragma unroll
     for (int p = 0; p < kPasses; ++p) {
       const int r = (p * S::kThreads + threadIdx.x) / 8;

@@ -17,6 +17,9 @@
 //   cta    one thread block per row, rows <= 1024 packs (16 KiB of bf16),
 //          1, 2 or 4 packs per thread; one barrier per row (double-buffered
 //          partial sums). The default for every row up to 16 KiB.
+//   staged a block per row, the row and the weight brought into shared memory
+//          by the TMA engine (cp.async.bulk, mbarrier completion); 4-16 KiB
+//          rows in calls of 16-128 MiB.
 //   bulk   persistent blocks, rows staged through shared memory by the TMA
 //          engine (cp.async.bulk, mbarrier completion); rows of 16-32 KiB.
 //   wide   one thread block per row, any 16-byte-aligned row; two passes
@@ -36,6 +39,7 @@ namespace sm120n {
 // Bounded waits that expired in the pipelined kernels of this file since the
 // last reset (see sm120n_get_device_faults). Zero in correct operation.
 __device__ unsigned int g_expired_waits = 0;
+static_assert(kDefaultWaitPolls == kMaxBarrierPolls, "host and device wait bounds agree");
 
 namespace {
 
@@ -49,6 +53,7 @@ struct RowArgs {
   int64_t rows;
   int hidden;
   float epsilon;
+  uint32_t wait_polls;  // poll limit of waits on bulk copies (from the host's setting)
 };
 
 // ---- warp family -----------------------------------------------------------
@@ -287,7 +292,7 @@ __global__ void __launch_bounds__(1024) row_norm_bulk_kernel(RowArgs<T> a, int s
   for (int64_t i = 0; i < my_rows; ++i) {
     const int s = static_cast<int>(i % stages);
     const uint32_t phase = static_cast<uint32_t>((i / stages) & 1);
-    const bool arrived = mbarrier_wait_bounded(&stage_full[s], phase);
+    const bool arrived = mbarrier_wait_limited(&stage_full[s], phase, a.wait_polls);
     const unsigned char* stage = stage_memory + static_cast<size_t>(s) * stage_bytes;
     uint4 v[kPacksPerThread];
     float2 acc = make_float2(0.0f, 0.0f);
@@ -334,10 +339,84 @@ __global__ void __launch_bounds__(1024) row_norm_bulk_kernel(RowArgs<T> a, int s
   }
 }
 
+// ---- staged family: a block per row, the row brought in by the TMA engine ---
+// For calls whose rows fit on the device in about one wave of these blocks.
+// Right after the upstream wait thread 0 copies the block's input row,
+// residual row and the weight into shared memory with bulk copies, so a
+// launch's reads are all in flight at once and no block waits for a second
+// pass; data in flight occupy shared memory instead of registers, which keeps
+// 2048 / kMaxThreads blocks resident per SM (the persistent register kernel
+// fits half as many). Packs are assigned to threads as in the cta family with
+// the same block size, so results are bit-identical to it.
+template <typename T, bool kAdd, int kPacksPerThread, int kMaxThreads>
+__global__ void __launch_bounds__(kMaxThreads, 2048 / kMaxThreads)
+    row_norm_staged_kernel(RowArgs<T> a) {
+  constexpr int E = Pack<T>::kElems;
+  extern __shared__ __align__(128) unsigned char staged[];  // input | residual | weight
+  __shared__ __align__(8) uint64_t landed;
+  __shared__ float partial[2][kWarpSize];
+  const int64_t row = blockIdx.x;
+  const int packs = a.hidden / E;
+  const uint32_t row_bytes = static_cast<uint32_t>(a.hidden) * sizeof(T);
+  unsigned char* input_s = staged;
+  unsigned char* residual_s = staged + row_bytes;
+  unsigned char* weight_s = staged + (kAdd ? 2 : 1) * row_bytes;
+  prefetch_first_row<T, kAdd>(a, row);
+  if (threadIdx.x == 0) {
+    mbarrier_init(&landed, 1);
+    fence_mbarrier_init();
+  }
+  __syncthreads();
+  wait_for_upstream_grid();
+  release_downstream_grid();
+  const int64_t base = row * a.hidden;
+  if (threadIdx.x == 0) {
+    mbarrier_arrive_expect_tx(&landed, (kAdd ? 3 : 2) * row_bytes);
+    bulk_load(input_s, a.input + base, row_bytes, &landed);
+    if constexpr (kAdd) bulk_load(residual_s, a.residual + base, row_bytes, &landed);
+    bulk_load(weight_s, a.weight, row_bytes, &landed);
+  }
+  const bool arrived = mbarrier_wait_limited(&landed, 0, a.wait_polls);
+  if (__syncthreads_or(!arrived)) {
+    // The copies did not land within the limit: record it, wait (with the
+    // full bound) for them to finish before the block's shared memory is
+    // released, and leave the row.
+    if (threadIdx.x == 0) {
+      atomicAdd(&g_expired_waits, 1u);
+      mbarrier_wait_bounded(&landed, 0);
+    }
+    __syncthreads();
+    return;
+  }
+  uint4 s[kPacksPerThread];
+  float2 acc = make_float2(0.0f, 0.0f);
+#pragma unroll
+  for (int k = 0; k < kPacksPerThread; ++k) {
+    const int c = threadIdx.x + k * blockDim.x;
+    if (c < packs) {
+      uint4 r;
+      if constexpr (kAdd) r = load16_shared(residual_s + static_cast<uint32_t>(c) * 16);
+      s[k] = combine_pack<T, kAdd>(load16_shared(input_s + static_cast<uint32_t>(c) * 16), r, acc);
+      if constexpr (kAdd) store16(a.residual_output + base + static_cast<int64_t>(c) * E, s[k]);
+    }
+  }
+  const float inv =
+      inverse_rms(block_allreduce_sum(__fadd_rn(acc.x, acc.y), partial, 0), static_cast<float>(a.hidden),
+                  a.epsilon);
+#pragma unroll
+  for (int k = 0; k < kPacksPerThread; ++k) {
+    const int c = threadIdx.x + k * blockDim.x;
+    if (c < packs) {
+      store16(a.output + base + static_cast<int64_t>(c) * E,
+              normalise_pack<T>(s[k], load16_shared(weight_s + static_cast<uint32_t>(c) * 16), inv));
+    }
+  }
+}
+
 // ---------------------------------------------------------------------------
 // Host-side dispatch
 // ---------------------------------------------------------------------------
-enum class Family { kAuto, kWarp, kCta, kCtaOnePack, kWide, kBulk, kScalar };
+enum class Family { kAuto, kWarp, kCta, kCtaOnePack, kWide, kBulk, kScalar, kStaged };
 
 // Launch shape of the bulk family, or false when a row does not fit.
 struct BulkPlan {
@@ -425,6 +504,17 @@ int launch_bulk(const RowArgs<T>& a, const BulkPlan& plan, cudaStream_t stream) 
                 a, plan.stages);
 }
 
+// A block per row (rows <= INT32_MAX), two packs per thread, the row staged
+// in `smem` bytes of shared memory.
+template <typename T, bool kAdd, int kMaxThreads>
+int launch_staged(const RowArgs<T>& a, int threads, cudaStream_t stream) {
+  auto kernel = row_norm_staged_kernel<T, kAdd, 2, kMaxThreads>;
+  const size_t smem = static_cast<size_t>(kAdd ? 3 : 2) * a.hidden * sizeof(T);
+  const int rc = allow_dynamic_smem(reinterpret_cast<const void*>(kernel), smem);
+  if (rc != SM120N_OK) return rc;
+  return launch(kernel, dim3(static_cast<unsigned>(a.rows)), dim3(threads), smem, stream, a);
+}
+
 inline int round_up_warps(int64_t threads) {
   return static_cast<int>((threads + kWarpSize - 1) / kWarpSize * kWarpSize);
 }
@@ -452,7 +542,17 @@ int run_rows(const RowArgs<T>& a, Family family, cudaStream_t stream) {
     int rc = current_device_info(&dev);
     if (rc != SM120N_OK) return rc;
     many_rows = a.rows >= 8 * static_cast<int64_t>(dev.sm_count);
-    if (packs <= 256) {
+    const int64_t input_bytes = a.rows * static_cast<int64_t>(a.hidden) * sizeof(T);
+    if (packs >= 256 && packs <= 1024 && input_bytes >= (int64_t{16} << 20) &&
+        input_bytes <= (int64_t{128} << 20)) {
+      // 4-16 KiB rows, 16-128 MiB of input: rows staged in shared memory, a
+      // block per row (bf16 2048 x 4096: 13.6-13.8 us against 15.0-15.1;
+      // 4096 x 4096: 26.8-27.7 against 28.7; 1024 x 8192: 13.7-14.0 against
+      // 14.5-14.9; 4096 x 2048: 13.7 against 14.2-14.4). Below 16 MiB the
+      // register kernels win (1024 x 4096: 7.3 against 7.1 us); far above,
+      // the four-pack kernel matches it (16384 x 8192: 162 us both).
+      family = Family::kStaged;
+    } else if (packs <= 256) {
       family = a.rows >= 1024 ? Family::kCta : Family::kCtaOnePack;
     } else if (packs <= 1024) {
       family = Family::kCta;
@@ -466,6 +566,7 @@ int run_rows(const RowArgs<T>& a, Family family, cudaStream_t stream) {
   if ((family == Family::kCta || family == Family::kCtaOnePack) && packs > 1024) {
     family = Family::kWide;
   }
+  if (family == Family::kStaged && (packs > 1024 || a.rows > INT32_MAX)) family = Family::kCta;
 
   switch (family) {
     case Family::kWarp:
@@ -482,6 +583,11 @@ int run_rows(const RowArgs<T>& a, Family family, cudaStream_t stream) {
       // Two packs per thread: 32+ bytes of loads in flight per thread with a
       // modest register budget.
       return launch_cta<T, kAdd, 2, 512>(a, round_up_warps((packs + 1) / 2), stream);
+    }
+    case Family::kStaged: {
+      const int threads = round_up_warps((packs + 1) / 2);
+      if (threads <= 256) return launch_staged<T, kAdd, 256>(a, threads, stream);
+      return launch_staged<T, kAdd, 512>(a, threads, stream);
     }
     case Family::kBulk: {
       size_t block_smem = 0;
@@ -526,21 +632,22 @@ int run_rows_typed(int dtype, const void* input, const void* residual, const voi
       RowArgs<float> a{static_cast<const float*>(input), static_cast<const float*>(residual),
                        static_cast<const float*>(weight), static_cast<float*>(output),
                        static_cast<float*>(residual_output), rows, static_cast<int>(hidden),
-                       epsilon};
+                       epsilon, wait_poll_limit()};
       return run_rows<float, kAdd>(a, family, stream);
     }
     case SM120N_F16: {
       RowArgs<__half> a{static_cast<const __half*>(input), static_cast<const __half*>(residual),
                         static_cast<const __half*>(weight), static_cast<__half*>(output),
                         static_cast<__half*>(residual_output), rows, static_cast<int>(hidden),
-                        epsilon};
+                        epsilon, wait_poll_limit()};
       return run_rows<__half, kAdd>(a, family, stream);
     }
     default: {
       using B = __nv_bfloat16;
       RowArgs<B> a{static_cast<const B*>(input), static_cast<const B*>(residual),
                    static_cast<const B*>(weight), static_cast<B*>(output),
-                   static_cast<B*>(residual_output), rows, static_cast<int>(hidden), epsilon};
+                   static_cast<B*>(residual_output), rows, static_cast<int>(hidden), epsilon,
+                   wait_poll_limit()};
       return run_rows<B, kAdd>(a, family, stream);
     }
   }

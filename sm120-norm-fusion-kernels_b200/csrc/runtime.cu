@@ -15,6 +15,7 @@ namespace {
 
 thread_local std::string g_last_error;
 std::atomic<bool> g_programmatic_launch{true};
+std::atomic<uint32_t> g_wait_polls{kDefaultWaitPolls};
 
 constexpr int kMaxDevices = 64;
 std::mutex g_cache_mutex;
@@ -38,6 +39,8 @@ int fail(int status, const char* fmt, ...) {
 void clear_error() { g_last_error.clear(); }
 
 bool programmatic_launch_enabled() { return g_programmatic_launch.load(std::memory_order_relaxed); }
+
+uint32_t wait_poll_limit() { return g_wait_polls.load(std::memory_order_relaxed); }
 
 int current_device_info(DeviceInfo* info) {
   int device = 0;
@@ -153,5 +156,13 @@ const char* sm120n_status_string(int status) {
 void sm120n_set_programmatic_launch(int enabled) { sm120n::g_programmatic_launch.store(enabled != 0); }
 
 int sm120n_get_programmatic_launch(void) { return sm120n::g_programmatic_launch.load() ? 1 : 0; }
+
+void sm120n_set_wait_limit(uint32_t polls) {
+  sm120n::g_wait_polls.store(polls == 0 || polls > sm120n::kDefaultWaitPolls
+                                 ? sm120n::kDefaultWaitPolls
+                                 : polls);
+}
+
+uint32_t sm120n_get_wait_limit(void) { return sm120n::g_wait_polls.load(); }
 
 }  // extern "C"

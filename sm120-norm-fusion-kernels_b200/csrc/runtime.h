@@ -21,6 +21,12 @@ void clear_error();
 
 bool programmatic_launch_enabled();
 
+// Polls a kernel makes while waiting for its own bulk copies to land before
+// it records an expired wait (sm120n_set_wait_limit; kernels receive it as an
+// argument). The default is far beyond any real copy.
+constexpr uint32_t kDefaultWaitPolls = 1u << 22;
+uint32_t wait_poll_limit();
+
 struct DeviceInfo {
   int device = -1;
   int sm_count = 0;

@@ -74,6 +74,8 @@ SIGNATURES: dict[str, tuple[list, object]] = {
     "sm120n_get_programmatic_launch": ([], _i32),
     "sm120n_get_device_faults": ([ctypes.POINTER(ctypes.c_uint32)], _i32),
     "sm120n_reset_device_faults": ([], _i32),
+    "sm120n_set_wait_limit": ([ctypes.c_uint32], None),
+    "sm120n_get_wait_limit": ([], ctypes.c_uint32),
     "sm120n_rms_norm": ([_vp, _vp, _vp, _i64, _i64, _i32, _f32, _i32, _vp], _i32),
     "sm120n_fused_add_rms_norm": ([_vp, _vp, _vp, _vp, _vp, _i64, _i64, _i32, _f32, _i32, _vp], _i32),
     "sm120n_fused_qk_rms_norm_rope": (
@@ -137,6 +139,34 @@ def device_faults() -> int:
 
 def reset_device_faults() -> None:
     _check(load().sm120n_reset_device_faults())
+
+
+class DeviceFaultError(RuntimeError):
+    """A kernel gave up waiting on its own asynchronous copies and left rows
+    unwritten (see :func:`check_device_faults`)."""
+
+
+def check_device_faults(reset: bool = True) -> None:
+    """Raise :class:`DeviceFaultError` when a bounded wait expired on the
+    current device since the last reset (synchronises the device; the
+    operators themselves stay asynchronous and never read the counter). With
+    ``reset`` the counter is cleared before raising."""
+    count = device_faults()
+    if count:
+        if reset:
+            reset_device_faults()
+        raise DeviceFaultError(f"{count} bounded wait(s) on asynchronous copies expired; the "
+                               "affected rows of those calls were not written")
+
+
+def set_wait_limit(polls: int) -> None:
+    """Diagnostic: polls a kernel makes while waiting for its own bulk copies
+    before it records an expired wait (0 restores the default)."""
+    load().sm120n_set_wait_limit(int(polls))
+
+
+def wait_limit() -> int:
+    return int(load().sm120n_get_wait_limit())
 
 
 def rms_norm(input_ptr, weight_ptr, output_ptr, rows, hidden_size, dtype, epsilon=1e-6,

@@ -148,6 +148,30 @@ def assert_rope_close(actual: torch.Tensor, expected: torch.Tensor, bound: torch
             f"{e.flatten()[idx].item()}, propagation bound {bound.flatten()[idx].item()})")
 
 
+def strict_rope_violations(actual: torch.Tensor, expected: torch.Tensor, normed: torch.Tensor,
+                           positions: torch.Tensor, cos_sin: torch.Tensor) -> torch.Tensor:
+    """Mask of RoPE outputs outside the strict bar |dy| <= 1 ulp(max(|n_i c_i|,
+    |n_j s_i|)) (output i of a half-split pair (i, j): y_i = n_i c_i - n_j s_i,
+    y_j = n_j c_i + n_i s_i), ulps of the activation dtype. `normed` is the
+    oracle's n = round(round(x * inv_rms) * w) for [T, H, D] heads. The
+    propagated bar above is the one every output must meet; this stricter
+    one is reported as a count, since a different fp32 summation order
+    legitimately flips the first rounding of a few elements per million."""
+    dtype = expected.dtype
+    n = normed.detach().cpu().to(torch.float64)
+    rotary = cos_sin.shape[-1]
+    half = rotary // 2
+    rows = cos_sin.detach().cpu().reshape(-1, rotary).to(torch.float64)[positions.cpu().long()]
+    c, s = rows[:, None, :half], rows[:, None, half:]
+    n1, n2 = n[..., :half], n[..., half:rotary]
+    first = torch.maximum((n1 * c).abs(), (n2 * s).abs())
+    second = torch.maximum((n2 * c).abs(), (n1 * s).abs())
+    scale = torch.cat((first, second), dim=-1)
+    a = actual.detach().cpu().to(torch.float64)[..., :rotary]
+    e = expected.detach().cpu().to(torch.float64)[..., :rotary]
+    return (a - e).abs() > ulp_at(scale, dtype)
+
+
 def load_golden(name: str) -> dict:
     """Fixture `name` as a dict of CPU tensors (bf16 restored from raw bits)."""
     with np.load(GOLDEN / f"{name}.npz") as data:

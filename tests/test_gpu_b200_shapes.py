@@ -213,3 +213,31 @@ def test_qk_more_tokens_than_a_grid_dimension():
     fused_qk_rms_norm_rope(q, k, qw, kw, pos, cache)
     check_rope(q.cpu(), eq, q0, qw, pos, cache, what="query")
     check_rope(k.cpu(), ek, k0, kw, pos, cache, what="key")
+
+
+# ---- rows staged in shared memory (16-128 MiB calls of 4-16 KiB rows) ------------
+
+@pytest.mark.parametrize("rows,hidden,dtype", [
+    (2048, 4096, torch.bfloat16), (2048, 4096, torch.float16), (4096, 2048, torch.bfloat16),
+    (1024, 8192, torch.float16), (1024, 4096, torch.float32), (8192, 8192, torch.bfloat16)])
+def test_staged_rows_match_the_oracle_and_version_2(rows, hidden, dtype):
+    """The staged kernel (auto dispatch at these sizes) against the oracle on a
+    sample of rows and, bit for bit on every row, against version 2 (the
+    register kernel with the same threads and packs per thread)."""
+    g = gen(rows + hidden)
+    x = normal((rows, hidden), dtype, g)
+    r = normal((rows, hidden), dtype, g)
+    w = normal((hidden,), dtype, g, 1.0, 0.1)
+    sample = torch.randperm(rows, generator=torch.Generator().manual_seed(rows))[:256].cuda()
+    expected, expected_res = expect_fused_add(x[sample], r[sample], w)
+    x2, r2 = x.clone(), r.clone()
+    fused_add_rms_norm_inplace(x, r, w)
+    fused_add_rms_norm_inplace(x2, r2, w, version=2)
+    assert_bitwise_equal(r[sample], expected_res, what="residual (sampled rows)")
+    check_norm(x[sample].cpu(), expected, what="output (sampled rows)")
+    assert_bitwise_equal(r, r2, what="residual vs version 2")
+    assert_bitwise_equal(x, x2, what="output vs version 2")
+    # plain RMSNorm at the same size: oracle on the sample, version 1 bit for bit
+    y = rms_norm(r, w)
+    assert_bitwise_equal(y, rms_norm(r, w, version=1), what="rms_norm vs version 1")
+    check_norm(y[sample].cpu(), expect_rms_norm(r[sample], w), what="rms_norm (sampled rows)")

@@ -22,11 +22,11 @@ def header_symbols() -> set[str]:
 def test_library_loads_and_exports_every_declared_symbol():
     lib = capi.load()
     declared = header_symbols()
-    assert len(declared) == 15, declared
+    assert len(declared) == 17, declared
     for name in declared:
         assert hasattr(lib, name), name
     assert declared == set(capi.SIGNATURES), "capi.SIGNATURES must bind exactly the header"
-    assert capi.abi_version() == 4
+    assert capi.abi_version() == 5
 
 
 def test_library_exports_nothing_else():
@@ -166,3 +166,18 @@ def test_reference_exports_match_the_oracle_on_cpu():
     c, d = oracle.fused_add_rms_norm(x, r, w)
     assert torch.equal(b, d)
     assert_ulp_close(c, a)
+
+
+def test_wait_limit_setting_clamps_and_restores():
+    default = capi.wait_limit()
+    assert default == 1 << 22
+    try:
+        capi.set_wait_limit(3)
+        assert capi.wait_limit() == 3
+        capi.set_wait_limit(1 << 30)  # above the default: clamped to it
+        assert capi.wait_limit() == default
+        capi.set_wait_limit(5)
+        capi.set_wait_limit(0)  # 0 restores the default
+        assert capi.wait_limit() == default
+    finally:
+        capi.set_wait_limit(0)
