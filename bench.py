@@ -114,7 +114,7 @@ class Dist:
 
             import torch.distributed as dist
             torch.cuda.set_device(self.local_rank)
-            dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
+            dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=180),
                                     device_id=torch.device("cuda", self.local_rank))
             self.pg = dist
         else:

@@ -1,8 +1,8 @@
-"""The sharded path on real GPUs: one process per GPU, no collective on the data
-path (NCCL only for a barrier). Each rank normalises its own rows and its own
-decode sequences (private paged cache, rank-local slots); the parent process
-checks the reassembled result against the oracle. Skipped with fewer than two
-GPUs."""
+"""The sharded path on real GPUs: one process per visible GPU, no collective on
+the data path (NCCL only for a barrier). Each rank normalises its own rows and
+its own decode sequences (private paged cache, rank-local slots); the parent
+process checks the reassembled result against the oracle. Skipped with fewer
+than two GPUs."""
 import os
 import socket
 
@@ -73,16 +73,16 @@ def _worker(rank, world, port, out_dir):
 
 
 @pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs two GPUs")
-def test_two_gpus_shard_rows_and_sequences(tmp_path):
+def test_all_gpus_shard_rows_and_sequences(tmp_path):
     from gpu_cases import check_norm, check_rope
     from numerics import assert_bitwise_equal
     from oracle import oracle
 
     oracle.build()
-    world = 2
+    world = torch.cuda.device_count()
     mp.spawn(_worker, args=(world, _free_port(), str(tmp_path)), nprocs=world, join=True)
     parts = [torch.load(tmp_path / f"rank{i}.pt") for i in range(world)]
-    assert [p["device"] for p in parts] == [0, 1]
+    assert [p["device"] for p in parts] == list(range(world))
     x, r, w, q, k, v, qw, kw, pos, cache = _inputs()
     want_x, want_r = oracle.fused_add_rms_norm(x, r, w)
     assert_bitwise_equal(torch.cat([p["r"] for p in parts]), want_r, what="residual")
