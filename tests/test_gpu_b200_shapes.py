@@ -241,3 +241,22 @@ def test_staged_rows_match_the_oracle_and_version_2(rows, hidden, dtype):
     y = rms_norm(r, w)
     assert_bitwise_equal(y, rms_norm(r, w, version=1), what="rms_norm vs version 1")
     check_norm(y[sample].cpu(), expect_rms_norm(r[sample], w), what="rms_norm (sampled rows)")
+
+
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
+def test_staged_rows_out_of_place(dtype):
+    """The staged kernel writing separate output / residual-output buffers
+    (fused_add_rms_norm_out, fused_add_rms_norm) gives the in-place bits and
+    leaves its inputs untouched."""
+    g = gen(4096 + 2048)
+    x = normal((2048, 4096), dtype, g)
+    r = normal((2048, 4096), dtype, g)
+    w = normal((4096,), dtype, g, 1.0, 0.1)
+    x0, r0 = x.clone(), r.clone()
+    out, res = torch.empty_like(x), torch.empty_like(x)
+    fused_add_rms_norm_out(x, r, w, out, res)
+    assert_bitwise_equal(x, x0, what="input untouched")
+    assert_bitwise_equal(r, r0, what="residual untouched")
+    fused_add_rms_norm_inplace(x, r, w)
+    assert_bitwise_equal(out, x, what="output vs in place")
+    assert_bitwise_equal(res, r, what="residual output vs in place")
