@@ -1207,7 +1207,7 @@ def engine_suite(flush: Flusher, dist: Dist, args) -> dict:
         positions = torch.randperm(shape.max_positions, generator=cpu_g)[:batch].cuda()
         slots = torch.randperm(blocks * 16, generator=cpu_g)[:batch].to(torch.int32).cuda()
         row = {}
-        ours = DecodeGraph(layers, batch, cos_sin, kcs, vcs)
+        ours = DecodeGraph(layers, batch, cos_sin, kcs, vcs, fused_projection=False)
         ours.hidden.copy_(torch.randn(batch, shape.hidden, device="cuda", generator=g).to(bf))
         ours.residual.copy_(torch.randn(batch, shape.hidden, device="cuda", generator=g).to(bf))
         ours.positions.copy_(positions)

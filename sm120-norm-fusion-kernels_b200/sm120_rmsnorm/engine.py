@@ -113,18 +113,23 @@ class DecodeGraph:
     which are not part of this path), so every layer reads fresh data.
 
     Fill ``hidden``, ``residual``, ``positions`` and ``slot_mapping`` in
-    place, then ``replay()``.
+    place, then ``replay()``. ``fused_projection`` None picks the fused
+    projection where it measured faster (:meth:`fused_projection_pays`).
     """
 
     def __init__(self, layers: list[Qwen3AttentionPrologue], batch: int, cos_sin_cache,
                  key_caches: list[torch.Tensor], value_caches: list[torch.Tensor],
                  k_scale=None, v_scale=None, kv_cache_layout: str = "NHD",
-                 fused_projection: bool = False):
+                 fused_projection: bool | None = None):
         shape = layers[0].shape
         if shape.qkv_width < shape.hidden:
             raise ValueError("the stand-in between layers needs qkv_width >= hidden")
         dev = cos_sin_cache.device
         dtype = layers[0].qkv_weight.dtype
+        if fused_projection is None:
+            fused_projection = self.fused_projection_pays(batch, shape, dtype, key_caches,
+                                                          k_scale, kv_cache_layout)
+        self.fused_projection = fused_projection
         self.layers = layers
         self.hidden = torch.zeros(batch, shape.hidden, device=dev, dtype=dtype)
         self.residual = torch.zeros_like(self.hidden)
@@ -139,6 +144,18 @@ class DecodeGraph:
         self.graph = torch.cuda.CUDAGraph()
         with torch.cuda.graph(self.graph):
             self._run()
+
+    @staticmethod
+    def fused_projection_pays(batch, shape, dtype, key_caches, k_scale, kv_cache_layout) -> bool:
+        """Whether the projection with the fused Q/K epilogue is the faster
+        choice: up to four tokens, where it streams the weights on the CUDA
+        cores (a Qwen3-8B-shaped batch-1 step: 139.9 us against 166.8 us for
+        cuBLAS followed by the Q/K kernel), and only where it applies (bf16,
+        head_dim 128, dense bf16 NHD caches). From 16 tokens up cuBLAS followed
+        by the Q/K kernel measured faster."""
+        return (batch <= 4 and dtype == torch.bfloat16 and shape.head_dim == 128
+                and kv_cache_layout == "NHD" and k_scale is None
+                and all(c.dtype == torch.bfloat16 and c.is_contiguous() for c in key_caches))
 
     def _run(self):
         cos_sin, key_caches, value_caches, k_scale, v_scale, layout, fused = self._args

@@ -181,3 +181,19 @@ def test_wait_limit_setting_clamps_and_restores():
         assert capi.wait_limit() == default
     finally:
         capi.set_wait_limit(0)
+
+
+def test_engine_picks_the_fused_projection_only_where_it_pays():
+    from sm120_rmsnorm.engine import DecodeGraph, Qwen3AttentionShape
+
+    shape = Qwen3AttentionShape()
+    bf16_caches = [torch.zeros(4, 16, 8, 128, dtype=torch.bfloat16)]
+    pays = DecodeGraph.fused_projection_pays
+    assert pays(1, shape, torch.bfloat16, bf16_caches, None, "NHD")
+    assert pays(4, shape, torch.bfloat16, bf16_caches, None, "NHD")
+    assert not pays(16, shape, torch.bfloat16, bf16_caches, None, "NHD")  # cuBLAS + Q/K kernel
+    assert not pays(1, shape, torch.float16, bf16_caches, None, "NHD")    # bf16 only
+    assert not pays(1, shape, torch.bfloat16, bf16_caches, None, "HND")   # dense NHD only
+    fp8 = [torch.zeros(4, 16, 8, 128, dtype=torch.float8_e4m3fn)]
+    assert not pays(1, shape, torch.bfloat16, fp8, torch.ones(1), "NHD")  # no fp8 caches
+    assert not pays(1, Qwen3AttentionShape(head_dim=64), torch.bfloat16, bf16_caches, None, "NHD")
