@@ -147,6 +147,29 @@ __global__ void __launch_bounds__(256, sizeof(T) == 2 ? 5 : 2) head_cache_kernel
         prefetch_l2_line(a.slots + t0);
       }
     }
+    // The cos/sin rows of the first and last token of those two passes, from
+    // four lanes of the block's last warp, as in head_norm_rope_kernel: the
+    // position is read before the wait only to form an L2 request (bounds-
+    // checked; a stale value wastes the request, nothing else). Rows are
+    // 16-byte aligned on the vector path (rotary_dim is a multiple of 16).
+    const uint32_t lane_in_last = threadIdx.x - kWarpSize * (blockDim.x / kWarpSize - 1);
+    if (kVector && blockDim.x >= 2 * kWarpSize && lane_in_last < 4) {
+      const uint64_t pass_unit = (static_cast<uint64_t>(blockIdx.x) +
+                                  static_cast<uint64_t>(lane_in_last / 2) * gridDim.x) * per_block;
+      if (pass_unit < units) {
+        const uint32_t first = static_cast<uint32_t>(pass_unit);
+        const uint32_t t0 = divide(a.heads_div, first);
+        const uint32_t t = lane_in_last % 2 == 0 ? t0
+                           : divide(a.heads_div, min(units, first + per_block) - 1);
+        if (lane_in_last % 2 == 0 || t != t0) {
+          const int64_t position = a.positions[t];
+          if (position >= 0 && position < a.rope_positions) {
+            prefetch_l2(a.cos_sin + position * a.rotary_dim,
+                        static_cast<uint32_t>(a.rotary_dim) * sizeof(float));
+          }
+        }
+      }
+    }
   }
   wait_for_upstream_grid();
   release_downstream_grid();

@@ -121,6 +121,35 @@ __global__ void __launch_bounds__(256, sizeof(T) == 2 ? (kHoistWeights ? 4 : 5) 
         prefetch_l2_line(a.slots + t0);
       }
     }
+    // The cos/sin rows of the first and last token of those two passes, from
+    // four lanes of the block's last warp (the first warp's lanes issue the
+    // requests above). The position is read before the wait only to form an
+    // L2 request: a stale value costs a wasted request, never a wrong result
+    // (every load that uses data comes after the wait), and it is
+    // bounds-checked before the address is formed. Without this the rows are
+    // requested only after the position load that follows the wait: per call
+    // in bench.py's graphs (same box) batch-1 decode 1.75-1.81 us against
+    // 1.91-2.02, B = 64 2.02-2.05 against 2.35-2.37, B = 256 2.85-2.87
+    // against 3.20-3.21, B = 1024 6.86-6.90 against 7.07-7.20; prefills and
+    // the no-KV operator at T = 1..256 (positions already in L2) unchanged.
+    // (The bulk request needs the 16-byte-aligned table of the vector path.)
+    const uint32_t lane_in_last = threadIdx.x - kWarpSize * (blockDim.x / kWarpSize - 1);
+    if (kVector && blockDim.x >= 2 * kWarpSize && lane_in_last < 4) {
+      const uint64_t pass_unit = (static_cast<uint64_t>(blockIdx.x) +
+                                  static_cast<uint64_t>(lane_in_last / 2) * gridDim.x) * per_block;
+      if (pass_unit < units) {
+        const uint32_t first = static_cast<uint32_t>(pass_unit);
+        const uint32_t t0 = divide(a.heads_div, first);
+        const uint32_t t = lane_in_last % 2 == 0 ? t0
+                           : divide(a.heads_div, min(units, first + per_block) - 1);
+        if (lane_in_last % 2 == 0 || t != t0) {
+          const int64_t position = a.positions[t];
+          if (position >= 0 && position < a.rope_positions) {
+            prefetch_l2(a.cos_sin + position * kHeadDim, kHeadDim * sizeof(float));
+          }
+        }
+      }
+    }
   }
   wait_for_upstream_grid();
   release_downstream_grid();
