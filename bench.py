@@ -281,13 +281,18 @@ def time_graph(graph, flush: "Flusher", reps: int) -> float:
     return total / reps
 
 
-def time_calls(calls, flush: "Flusher", reps: int) -> tuple[float, str]:
+def time_calls(calls, flush: "Flusher", reps: int, eager_fallback: bool = False
+               ) -> tuple[float, str]:
     """us per call of `calls` (R calls on R distinct buffer sets) by the graph
-    protocol; calls that cannot be captured in a CUDA graph (some library
-    comparators) are timed as an eager back-to-back loop after the same flush."""
+    protocol. With `eager_fallback` (library comparators only), calls that
+    cannot be captured in a CUDA graph are timed as an eager back-to-back loop
+    after the same flush; this package's own calls always capture, and a
+    failure there propagates."""
     try:
         graph, _ = capture(calls)
-    except Exception:  # noqa: BLE001 - comparators only; our own calls capture
+    except Exception:  # noqa: BLE001 - re-raised unless this is a comparator
+        if not eager_fallback:
+            raise
         torch.cuda.synchronize()
         total = 0.0
         for _ in range(reps):
@@ -534,7 +539,7 @@ class PerConfig:
                 continue
             try:
                 calls = make()
-                us, how = time_calls(calls, self.flush, self.reps)
+                us, how = time_calls(calls, self.flush, self.reps, eager_fallback=True)
                 out[name] = round(us, 2) if how == "graph" else [round(us, 2), how]
                 del calls
             except Exception as e:  # noqa: BLE001 - comparators may be unavailable
