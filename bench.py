@@ -748,6 +748,100 @@ class PerConfig:
             self.put(f"qk (no kv) bf16 T={t} 16/8", us, nbytes, cmp=cmp)
             del sets, keep
 
+    def engine_formats(self):
+        """The engine-side extensions at their prefill / decode sizes beside
+        vLLM's kernels doing the same work (N = 1 only): the generalised Q/K
+        norm + RoPE + cache store on strided QKV views (bf16 and fp8 NHD
+        caches), and residual add + RMSNorm with fp8 and NVFP4 outputs."""
+        from sm120_rmsnorm import extensions as ext
+
+        bf = torch.bfloat16
+        g, cpu_g = self.g, self.cpu_g
+        vllm = vllm_ops()
+        one = torch.ones(1, device="cuda")
+        qw = (1 + 0.1 * torch.randn(128, device="cuda", generator=g)).to(bf)
+        kw = (1 + 0.1 * torch.randn(128, device="cuda", generator=g)).to(bf)
+        cache_bf = self.cache.to(bf)
+        for name, b, hq, hk, blocks, fp8, contiguous in (
+                ("ext qk_cache prefill 32768 tok 64/8 strided qkv, bf16 NHD cache",
+                 32768, 64, 8, 2048, False, True),
+                ("ext qk_cache decode B=1024 32/8 strided qkv, fp8 NHD cache",
+                 1024, 32, 8, 65536, True, False)):
+            nbytes = qk_cache_bytes(b, hq, hk, 2, cache_elem=1 if fp8 else 2)
+            kc = torch.zeros(blocks, 16, hk, 128, device="cuda",
+                             dtype=torch.float8_e4m3fn if fp8 else bf)
+            vc = torch.zeros_like(kc)
+            sets = []
+            all_slots = torch.randperm(blocks * 16, generator=cpu_g)
+            for i in range(sets_for(nbytes)):
+                qkv = torch.randn(b, (hq + 2 * hk) * 128, device="cuda", generator=g).to(bf)
+                if contiguous:
+                    pos = torch.arange(b, device="cuda")
+                    slots = torch.arange(b, device="cuda", dtype=torch.int32)
+                else:
+                    pos = torch.randperm(32768, generator=cpu_g)[:b].cuda()
+                    slots = all_slots[i * b:(i + 1) * b].to(torch.int32).cuda()
+                sets.append((qkv, qkv[:, :hq * 128].view(b, hq, 128),
+                             qkv[:, hq * 128:(hq + hk) * 128].view(b, hk, 128),
+                             qkv[:, (hq + hk) * 128:].view(b, hk, 128), pos, slots))
+            scales = (one, one) if fp8 else (None, None)
+            us = self.us([lambda s=s: ext.qk_norm_rope_cache_(
+                s[1], s[2], s[3], qw, kw, s[4], self.cache, kc, vc, s[5], *scales)
+                for s in sets])
+            cmp = {}
+            if vllm is not None:
+                C, cache_ops = vllm
+                vkc = torch.zeros(blocks, 16, hk, 128, device="cuda",
+                                  dtype=torch.uint8 if fp8 else bf)
+                vvc = torch.zeros_like(vkc)
+                kind = "fp8" if fp8 else "auto"
+
+                def unfused(s):
+                    C.fused_qk_norm_rope(s[0], hq, hk, hk, 128, EPS, qw, kw, cache_bf, True, s[4])
+                    cache_ops.reshape_and_cache_flash(s[2], s[3], vkc, vvc, s[5].long(), kind,
+                                                      one, one)
+
+                cmp = self.comparators({"vllm_qk_norm_rope_and_reshape_and_cache":
+                                        lambda: [lambda s=s: unfused(s) for s in sets]})
+                del vkc, vvc
+            self.put(name, us, nbytes, cmp=cmp)
+            del sets, kc, vc
+            torch.cuda.empty_cache()
+
+        t, h = HEADLINE_ROWS, HEADLINE_HIDDEN
+        w = (1 + 0.1 * torch.randn(h, device="cuda", generator=g)).to(bf)
+        x = torch.randn(t, h, device="cuda", generator=g).to(bf)
+        r = torch.randn(t, h, device="cuda", generator=g).to(bf)
+        scale = torch.full((1,), 0.05, device="cuda")
+        q8 = torch.empty(t, h, device="cuda", dtype=torch.float8_e4m3fn)
+        nbytes = t * h * 2 * 3 + t * h + h * 2
+        us = self.us([lambda: ext.fused_add_rms_norm_static_fp8_quant(q8, x, r, w, scale, EPS)])
+        cmp = {}
+        if vllm is not None:
+            cmp = self.comparators({"vllm": lambda: [
+                lambda: vllm[0].fused_add_rms_norm_static_fp8_quant(q8, x, r, w, scale, EPS)]})
+        self.put("ext fused add + RMSNorm + static fp8, 65536x8192", us, nbytes, cmp=cmp)
+        del q8
+        gscale = torch.full((1,), 448.0 * 6.0 / 8.0, device="cuda")
+        q4 = torch.empty(t, h // 2, device="cuda", dtype=torch.uint8)
+        sc = torch.empty(ext.nvfp4_scale_bytes(t, h), device="cuda", dtype=torch.uint8)
+        nbytes = t * h * 2 * 3 + t * h // 2 + t * h // 16 + h * 2
+        us = self.us([lambda: ext.rms_norm_nvfp4_quant(q4, sc, x, w, gscale, EPS, r)])
+        cmp = {}
+        if vllm is not None:
+            sc32 = sc.view(torch.int32)
+
+            def theirs():
+                vllm[0].fused_add_rms_norm(x, r, w, EPS)
+                vllm[0].scaled_fp4_quant.out(x, gscale, True, output=q4, output_scale=sc32)
+
+            cmp = self.comparators({"vllm_fused_add_rms_norm_and_scaled_fp4_quant":
+                                    lambda: [theirs]})
+        self.put("ext fused add + RMSNorm + NVFP4 (tiled scales), 65536x8192", us, nbytes,
+                 cmp=cmp)
+        del x, r, q4, sc
+        torch.cuda.empty_cache()
+
     def run(self, headline_us: float, headline_t1):
         d = self.dist
         self.rms_fp32()
@@ -767,6 +861,8 @@ class PerConfig:
         self.put("fused_add prefill bf16 65536x8192 (headline)", headline_us,
                  fused_bytes(HEADLINE_ROWS, HEADLINE_HIDDEN, 2), sharded=True, t1=headline_t1,
                  cmp=cmp)
+        if self.cmp_on:
+            self.engine_formats()
         return self.out
 
 
