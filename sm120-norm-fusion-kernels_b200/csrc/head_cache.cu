@@ -224,8 +224,10 @@ __global__ void __launch_bounds__(256, sizeof(T) == 2 ? 5 : 2) head_cache_kernel
         // Same-type caches read V whatever the slot holds, so that no load
         // waits on the slot (B = 1024 decode, bf16 cache: 8.24 us against
         // 8.52); fp8 caches keep the V registers free until the slot is known
-        // (the unconditional form spills there and the 32768-token prefill
-        // loses 1.5%).
+        // (read unconditionally, the general form spills and the 32768-token
+        // prefill loses 1.5%; the whole-head NEOX form does not spill but its
+        // prefill still loses 2.3%, 247.6 against 242.1 us, while its B = 1024
+        // decode gains 1%). The store below checks the slot's range itself.
         if (kCache == kSameType || (slot >= 0 && slot < a.cache_slots)) {
           const T* vh = a.value + static_cast<int64_t>(token) * a.value_stride +
                         static_cast<int64_t>(kv_head) * D;
@@ -262,8 +264,8 @@ __global__ void __launch_bounds__(256, sizeof(T) == 2 ? 5 : 2) head_cache_kernel
     }
     store_half<T, kVector>(head + off_a, y_a);
     store_half<T, kVector>(head + off_b, y_b);
-    // (query heads keep slot = -1; same-type caches check the range here)
-    if (kCache != kNoCache && slot >= 0 && (kCache != kSameType || slot < a.cache_slots)) {
+    // (query heads keep slot = -1; every slot outside the cache stores nothing)
+    if (kCache != kNoCache && slot >= 0 && slot < a.cache_slots) {
       const uint32_t block = static_cast<uint32_t>(slot) / a.block_size;
       const uint32_t offset = static_cast<uint32_t>(slot) - block * a.block_size;
       const int64_t base = static_cast<int64_t>(block) * a.block_stride +
