@@ -101,8 +101,12 @@ __device__ __forceinline__ float token_scale(float peak, const float* scale_ub) 
   return fmaxf(__fdiv_rn(peak, kFp8Max), kMinTokenScale);
 }
 
-template <typename T, bool kAdd, bool kDynamic, int kPacksPerThread, int kMaxThreads>
-__global__ void __launch_bounds__(kMaxThreads) norm_quant_cta_kernel(QuantArgs<T> a) {
+// kWeightsInRegisters: each thread keeps its weight packs in registers for the
+// whole launch; otherwise it reads them from L1 per row, which frees the
+// registers for more resident blocks (kMinBlocks per SM).
+template <typename T, bool kAdd, bool kDynamic, int kPacksPerThread, int kMaxThreads,
+          int kMinBlocks = 1, bool kWeightsInRegisters = true>
+__global__ void __launch_bounds__(kMaxThreads, kMinBlocks) norm_quant_cta_kernel(QuantArgs<T> a) {
   constexpr int E = Pack<T>::kElems;
   __shared__ float partial[2][kWarpSize];
   __shared__ float peaks[2][kWarpSize];
@@ -115,10 +119,12 @@ __global__ void __launch_bounds__(kMaxThreads) norm_quant_cta_kernel(QuantArgs<T
   const int packs = a.hidden / E;
   const float n = static_cast<float>(a.hidden);
   uint4 w[kPacksPerThread];
+  if constexpr (kWeightsInRegisters) {
 #pragma unroll
-  for (int i = 0; i < kPacksPerThread; ++i) {
-    const int c = threadIdx.x + i * blockDim.x;
-    if (c < packs) w[i] = load16(a.weight + static_cast<int64_t>(c) * E);
+    for (int i = 0; i < kPacksPerThread; ++i) {
+      const int c = threadIdx.x + i * blockDim.x;
+      if (c < packs) w[i] = load16(a.weight + static_cast<int64_t>(c) * E);
+    }
   }
   float inv_scale = 0.0f;
   if constexpr (!kDynamic) inv_scale = __frcp_rn(*a.scale);
@@ -152,7 +158,9 @@ __global__ void __launch_bounds__(kMaxThreads) norm_quant_cta_kernel(QuantArgs<T
     for (int i = 0; i < kPacksPerThread; ++i) {
       const int c = threadIdx.x + i * blockDim.x;
       if (c < packs) {
-        s[i] = normalise_pack<T>(s[i], w[i], inv);  // s now holds y
+        const uint4 wc =
+            kWeightsInRegisters ? w[i] : load16(a.weight + static_cast<int64_t>(c) * E);
+        s[i] = normalise_pack<T>(s[i], wc, inv);  // s now holds y
         if constexpr (kDynamic) peak = pack_abs_max<T>(s[i], peak);
       }
     }
@@ -280,10 +288,12 @@ int grid_for(Kernel kernel, int threads, int64_t rows, int* grid) {
 // `one_row_per_block`: a block per row, balanced by the block scheduler (the
 // better shape for many wide rows, as for the plain row kernels); otherwise a
 // persistent grid with a row loop.
-template <typename T, bool kAdd, bool kDynamic, int kPPT, int kMaxThreads>
+template <typename T, bool kAdd, bool kDynamic, int kPPT, int kMaxThreads, int kMinBlocks = 1,
+          bool kWeightsInRegisters = true>
 int launch_quant_cta(const QuantArgs<T>& a, int packs, cudaStream_t stream,
                      bool one_row_per_block = false) {
-  auto kernel = norm_quant_cta_kernel<T, kAdd, kDynamic, kPPT, kMaxThreads>;
+  auto kernel =
+      norm_quant_cta_kernel<T, kAdd, kDynamic, kPPT, kMaxThreads, kMinBlocks, kWeightsInRegisters>;
   const int threads = (((packs + kPPT - 1) / kPPT) + kWarpSize - 1) / kWarpSize * kWarpSize;
   int grid = 0;
   if (one_row_per_block && a.rows <= INT32_MAX) {
@@ -307,16 +317,23 @@ int run_quant(const QuantArgs<T>& a, cudaStream_t stream) {
   if (vectorisable && packs <= 4 * 512) {
     // Chosen from measurements on B200 (graphs of back-to-back calls on cold
     // data): rows wider than 512 packs with many rows run best as persistent
-    // 256-thread blocks holding four packs per thread (65536 x 8192 bf16 with
-    // the residual add: 569 us against 607 us with 512 threads of two packs);
-    // narrower or fewer rows keep two packs per thread.
+    // 256-thread blocks holding four packs per thread, reading the weight
+    // from L1 per row so that more blocks fit on an SM. With the residual
+    // add, three blocks per SM: 65536 x 8192 bf16 static 577 us (607 with the
+    // weight in registers at two blocks), dynamic 590 (667), fp16 static 577
+    // (615). Without it, four: static 306 us (402), dynamic 381 (488).
+    // Narrower or fewer rows keep two packs per thread.
     DeviceInfo dev;
     int rc = current_device_info(&dev);
     if (rc != SM120N_OK) return rc;
     const bool many_rows = a.rows >= 8 * static_cast<int64_t>(dev.sm_count);
     if (packs <= 256) return launch_quant_cta<T, kAdd, kDynamic, 1, 256>(a, packs, stream);
     if (many_rows && packs > 512 && packs <= 1024) {
-      return launch_quant_cta<T, kAdd, kDynamic, 4, 256>(a, packs, stream);
+      if constexpr (kAdd) {
+        return launch_quant_cta<T, kAdd, kDynamic, 4, 256, 3, false>(a, packs, stream);
+      } else {
+        return launch_quant_cta<T, kAdd, kDynamic, 4, 256, 4, false>(a, packs, stream);
+      }
     }
     if (packs <= 1024) return launch_quant_cta<T, kAdd, kDynamic, 2, 512>(a, packs, stream);
     return launch_quant_cta<T, kAdd, kDynamic, 4, 512>(a, packs, stream);

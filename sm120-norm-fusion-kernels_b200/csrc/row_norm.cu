@@ -30,6 +30,7 @@
 // families: each element is read before it is written and only by the thread
 // that writes it, and no pointer is declared __restrict__.
 #include <algorithm>
+#include <type_traits>
 
 #include "device_utils.cuh"
 #include "runtime.h"
@@ -110,8 +111,12 @@ __global__ void __launch_bounds__(256) row_norm_warp_kernel(RowArgs<T> a) {
 }
 
 // ---- cta family --------------------------------------------------------------
-template <typename T, bool kAdd, int kPacksPerThread, int kMaxThreads>
-__global__ void __launch_bounds__(kMaxThreads) row_norm_cta_kernel(RowArgs<T> a) {
+// kWeightsInRegisters: each thread keeps its weight packs in registers for the
+// whole launch; otherwise it reads them from L1 per row, which frees the
+// registers for more resident blocks (kMinBlocks per SM).
+template <typename T, bool kAdd, int kPacksPerThread, int kMaxThreads, int kMinBlocks = 1,
+          bool kWeightsInRegisters = true>
+__global__ void __launch_bounds__(kMaxThreads, kMinBlocks) row_norm_cta_kernel(RowArgs<T> a) {
   constexpr int E = Pack<T>::kElems;
   __shared__ float partial[2][kWarpSize];
   // Four packs per thread serve the many-row, bandwidth-bound calls, where the
@@ -126,10 +131,12 @@ __global__ void __launch_bounds__(kMaxThreads) row_norm_cta_kernel(RowArgs<T> a)
   const float n = static_cast<float>(a.hidden);
 
   uint4 w[kPacksPerThread];
+  if constexpr (kWeightsInRegisters) {
 #pragma unroll
-  for (int i = 0; i < kPacksPerThread; ++i) {
-    const int c = threadIdx.x + i * blockDim.x;
-    if (c < packs) w[i] = load16(a.weight + static_cast<int64_t>(c) * E);
+    for (int i = 0; i < kPacksPerThread; ++i) {
+      const int c = threadIdx.x + i * blockDim.x;
+      if (c < packs) w[i] = load16(a.weight + static_cast<int64_t>(c) * E);
+    }
   }
 
   int parity = 0;
@@ -164,7 +171,9 @@ __global__ void __launch_bounds__(kMaxThreads) row_norm_cta_kernel(RowArgs<T> a)
     for (int i = 0; i < kPacksPerThread; ++i) {
       const int c = threadIdx.x + i * blockDim.x;
       if (c < packs) {
-        store16(a.output + base + static_cast<int64_t>(c) * E, normalise_pack<T>(s[i], w[i], inv));
+        const uint4 wc =
+            kWeightsInRegisters ? w[i] : load16(a.weight + static_cast<int64_t>(c) * E);
+        store16(a.output + base + static_cast<int64_t>(c) * E, normalise_pack<T>(s[i], wc, inv));
       }
     }
   }
@@ -473,10 +482,12 @@ int launch_warp(const RowArgs<T>& a, cudaStream_t stream) {
 // `one_row_per_block`: a block per row and let the block scheduler balance
 // the waves (best for many rows: measured 620 us vs 682 us persistent on the
 // 65536 x 8192 bf16 prefill); otherwise a persistent grid with a row loop.
-template <typename T, bool kAdd, int kPacksPerThread, int kMaxThreads>
+template <typename T, bool kAdd, int kPacksPerThread, int kMaxThreads, int kMinBlocks = 1,
+          bool kWeightsInRegisters = true>
 int launch_cta(const RowArgs<T>& a, int threads, cudaStream_t stream,
                bool one_row_per_block = false) {
-  auto kernel = row_norm_cta_kernel<T, kAdd, kPacksPerThread, kMaxThreads>;
+  auto kernel =
+      row_norm_cta_kernel<T, kAdd, kPacksPerThread, kMaxThreads, kMinBlocks, kWeightsInRegisters>;
   int grid = 0;
   if (one_row_per_block && a.rows <= INT32_MAX) {
     grid = static_cast<int>(a.rows);
@@ -578,7 +589,20 @@ int run_rows(const RowArgs<T>& a, Family family, cudaStream_t stream) {
       return launch_cta<T, kAdd, 1, 1024>(a, round_up_warps(packs), stream);
     case Family::kCta: {
       if (many_rows && packs >= 512) {
-        return launch_cta<T, kAdd, 4, 256>(a, round_up_warps((packs + 3) / 4), stream, true);
+        // The weight is read from L1 per row rather than held in registers,
+        // which leaves room for more blocks per SM (bit-identical results).
+        // Measured on one B200, graphs of back-to-back calls on cold data,
+        // against the weight in registers: with the residual add at three
+        // blocks per SM, 65536 x 8192 bf16 620 us (663), fp16 619 (661),
+        // 16384 x 8192 bf16 163 (172); without it at four, 65536 x 8192 bf16
+        // 326 us (479), 65536 x 4096 bf16 161 (193).
+        if constexpr (kAdd) {
+          return launch_cta<T, kAdd, 4, 256, 3, false>(a, round_up_warps((packs + 3) / 4), stream,
+                                                       true);
+        } else {
+          return launch_cta<T, kAdd, 4, 256, 4, false>(a, round_up_warps((packs + 3) / 4), stream,
+                                                       true);
+        }
       }
       // Two packs per thread: 32+ bytes of loads in flight per thread with a
       // modest register budget.
