@@ -105,7 +105,7 @@ __device__ __forceinline__ float token_scale(float peak, const float* scale_ub) 
 // whole launch; otherwise it reads them from L1 per row, which frees the
 // registers for more resident blocks (kMinBlocks per SM).
 template <typename T, bool kAdd, bool kDynamic, int kPacksPerThread, int kMaxThreads,
-          int kMinBlocks = 1, bool kWeightsInRegisters = true>
+          int kMinBlocks = 0, bool kWeightsInRegisters = true>
 __global__ void __launch_bounds__(kMaxThreads, kMinBlocks) norm_quant_cta_kernel(QuantArgs<T> a) {
   constexpr int E = Pack<T>::kElems;
   __shared__ float partial[2][kWarpSize];
@@ -288,7 +288,7 @@ int grid_for(Kernel kernel, int threads, int64_t rows, int* grid) {
 // `one_row_per_block`: a block per row, balanced by the block scheduler (the
 // better shape for many wide rows, as for the plain row kernels); otherwise a
 // persistent grid with a row loop.
-template <typename T, bool kAdd, bool kDynamic, int kPPT, int kMaxThreads, int kMinBlocks = 1,
+template <typename T, bool kAdd, bool kDynamic, int kPPT, int kMaxThreads, int kMinBlocks = 0,
           bool kWeightsInRegisters = true>
 int launch_quant_cta(const QuantArgs<T>& a, int packs, cudaStream_t stream,
                      bool one_row_per_block = false) {

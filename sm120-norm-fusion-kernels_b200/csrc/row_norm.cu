@@ -114,7 +114,7 @@ __global__ void __launch_bounds__(256) row_norm_warp_kernel(RowArgs<T> a) {
 // kWeightsInRegisters: each thread keeps its weight packs in registers for the
 // whole launch; otherwise it reads them from L1 per row, which frees the
 // registers for more resident blocks (kMinBlocks per SM).
-template <typename T, bool kAdd, int kPacksPerThread, int kMaxThreads, int kMinBlocks = 1,
+template <typename T, bool kAdd, int kPacksPerThread, int kMaxThreads, int kMinBlocks = 0,
           bool kWeightsInRegisters = true>
 __global__ void __launch_bounds__(kMaxThreads, kMinBlocks) row_norm_cta_kernel(RowArgs<T> a) {
   constexpr int E = Pack<T>::kElems;
@@ -482,7 +482,7 @@ int launch_warp(const RowArgs<T>& a, cudaStream_t stream) {
 // `one_row_per_block`: a block per row and let the block scheduler balance
 // the waves (best for many rows: measured 620 us vs 682 us persistent on the
 // 65536 x 8192 bf16 prefill); otherwise a persistent grid with a row loop.
-template <typename T, bool kAdd, int kPacksPerThread, int kMaxThreads, int kMinBlocks = 1,
+template <typename T, bool kAdd, int kPacksPerThread, int kMaxThreads, int kMinBlocks = 0,
           bool kWeightsInRegisters = true>
 int launch_cta(const RowArgs<T>& a, int threads, cudaStream_t stream,
                bool one_row_per_block = false) {

@@ -66,7 +66,7 @@ def test_headline_rows_are_split_exactly(bench, world):
 def test_traffic_scales_the_committed_capture_by_rows(bench):
     full = bench.dram_traffic_per_launch(65536)
     quarter = bench.dram_traffic_per_launch(16384)
-    assert quarter == 1_018_850_816
+    assert quarter == 1_017_147_136
     assert full == 4 * quarter
     assert full < bench.fused_bytes(65536, 8192, 2)  # no re-reads
 
