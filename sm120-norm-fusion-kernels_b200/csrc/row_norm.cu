@@ -606,7 +606,21 @@ int run_rows(const RowArgs<T>& a, Family family, cudaStream_t stream) {
       }
       // Two packs per thread: 32+ bytes of loads in flight per thread with a
       // modest register budget.
-      return launch_cta<T, kAdd, 2, 512>(a, round_up_warps((packs + 1) / 2), stream);
+      const int threads = round_up_warps((packs + 1) / 2);
+      if (threads <= 256) {
+        // Where the grid of blocks holding the weight in registers cannot take
+        // every row at once, the weight is read from L1 per row instead: six
+        // 256-thread blocks fit per SM rather than four, so fewer blocks make
+        // a second pass (1024 x 4096 bf16 7.0 us against 7.25, 768 x 4096 5.6
+        // against 5.8; the same threads and packs, so the same sums). Where
+        // every row fits, the registers win: the weight's load then sits on
+        // each block's one critical path (512 x 4096 3.85 us against 4.3).
+        int grid = 0;
+        int rc = persistent_grid(row_norm_cta_kernel<T, kAdd, 2, 512>, threads, a.rows, &grid);
+        if (rc != SM120N_OK) return rc;
+        if (a.rows > grid) return launch_cta<T, kAdd, 2, 256, 6, false>(a, threads, stream);
+      }
+      return launch_cta<T, kAdd, 2, 512>(a, threads, stream);
     }
     case Family::kStaged: {
       const int threads = round_up_warps((packs + 1) / 2);
