@@ -23,6 +23,8 @@ from __future__ import annotations
 from pathlib import Path
 
 import numpy as np
+import math
+
 import torch
 
 GOLDEN = Path(__file__).resolve().parent / "golden"
@@ -55,13 +57,23 @@ def ulp_at(magnitude: torch.Tensor, dtype: torch.dtype) -> torch.Tensor:
     return torch.pow(2.0, exponent - MANTISSA_BITS[dtype])
 
 
-def default_norm_ulps(dtype: torch.dtype) -> int:
-    return 4 if dtype == torch.float32 else 1
+def default_norm_ulps(dtype: torch.dtype, row_length: int = 1024) -> int:
+    """Norm-output bar. 16-bit outputs: 1 ulp (the final rounding to the
+    activation dtype absorbs the fp32 sum-order difference). fp32 outputs:
+    4 ulp for rows of up to 1024 elements (the reference's fp32 workload), and
+    for longer rows 4 * ceil(sqrt(n / 1024)): the kernels and the oracle add
+    the n squares in different, equally valid fp32 orders, and the rounding
+    error of a sum of n positive terms grows with sqrt(n) (a different order
+    moves inv_rms, and so every output of the row, by that relative amount)."""
+    if dtype != torch.float32:
+        return 1
+    return 4 * max(1, math.ceil(math.sqrt(row_length / 1024)))
 
 
 def assert_ulp_close(actual: torch.Tensor, expected: torch.Tensor, max_ulp: int | None = None,
                      what: str = "") -> None:
-    max_ulp = default_norm_ulps(expected.dtype) if max_ulp is None else max_ulp
+    if max_ulp is None:
+        max_ulp = default_norm_ulps(expected.dtype, expected.shape[-1] if expected.dim() else 1)
     d = ulp_distance(actual, expected)
     worst = int(d.max()) if d.numel() else 0
     if worst > max_ulp:

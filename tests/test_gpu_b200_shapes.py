@@ -71,6 +71,24 @@ def test_fused_add_sweep_in_place(dtype, hidden, tokens, version):
     check_norm(x.cpu(), expected, what="output")
 
 
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16, torch.float32])
+@pytest.mark.parametrize("hidden", [2048, 2560, 3072, 4096])
+@pytest.mark.parametrize("tokens", [500, 600, 700, 900, 1200])
+def test_rows_around_the_resident_grid(dtype, hidden, tokens):
+    """Mid-size calls on either side of the point where the two-pack grid with
+    the weight in registers stops holding every row at once (above it the
+    weight is read from L1 at more blocks per SM)."""
+    g = gen(tokens * 13 + hidden)
+    x = normal((tokens, hidden), dtype, g)
+    r = normal((tokens, hidden), dtype, g)
+    w = normal((hidden,), dtype, g, 1.0, 0.1)
+    check_norm(rms_norm(x, w).cpu(), expect_rms_norm(x, w), what="rms_norm")
+    expected, expected_res = expect_fused_add(x, r, w)
+    fused_add_rms_norm_inplace(x, r, w)
+    assert_bitwise_equal(r, expected_res, what="residual")
+    check_norm(x.cpu(), expected, what="output")
+
+
 @pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
 @pytest.mark.parametrize("tokens", [1, 256, 1024])
 @pytest.mark.parametrize("version", [3, 4])
