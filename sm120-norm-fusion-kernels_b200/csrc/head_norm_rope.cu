@@ -298,7 +298,10 @@ int run_heads(HeadArgs<T> a, int threads_per_block, cudaStream_t stream) {
       if (rc != SM120N_OK) return rc;
       blocks = std::min<int64_t>(blocks, static_cast<int64_t>(dev.sm_count) * resident);
     } else {
-      blocks = (warps_needed * kWarpSize + threads - 1) / threads;
+      // At most 2^31 threads, so that the kernel's 32-bit warp index and
+      // warp count cannot wrap; the kernel's loop takes any remaining units.
+      blocks = std::min<int64_t>((warps_needed * kWarpSize + threads - 1) / threads,
+                                 (int64_t{1} << 31) / threads);
     }
     rc = launch(kernel, dim3(static_cast<unsigned>(std::max<int64_t>(blocks, 1))),
                 dim3(static_cast<unsigned>(threads)), 0, stream, c);
