@@ -56,10 +56,23 @@ struct Fp4Args {
   float epsilon;
 };
 
-__device__ __forceinline__ int64_t scale_offset(int64_t row, int block, int columns, bool tiled) {
-  if (!tiled) return row * columns + block;
-  const int64_t tile = (row / 128) * (columns / 4) + block / 4;
-  return tile * 512 + ((row % 32) * 4 + (row % 128) / 32) * 4 + block % 4;
+// Byte offset of block `block`'s scale in row `row`, split into a part that
+// depends on the row only and one that depends on the block only:
+//   row-major  row * columns + block
+//   tiled      tile (row / 128, block / 4) of 512 bytes, then
+//              ((row % 32) * 4 + (row % 128) / 32) * 4 + block % 4 inside it
+// (row and block are non-negative).
+__device__ __forceinline__ int64_t scale_row_offset(int64_t row, int columns, bool tiled) {
+  if (!tiled) return row * columns;
+  const uint64_t m = static_cast<uint64_t>(row);
+  return static_cast<int64_t>((m >> 7) * (static_cast<uint64_t>(columns) >> 2) * 512 +
+                              (((m & 31) << 2) + ((m & 127) >> 5)) * 4);
+}
+
+__device__ __forceinline__ int64_t scale_block_offset(int block, bool tiled) {
+  const uint32_t k = static_cast<uint32_t>(block);
+  return tiled ? static_cast<int64_t>(k >> 2) * 512 + static_cast<int64_t>(k & 3u)
+               : static_cast<int64_t>(k);
 }
 
 // r = g / s for the e4m3 code of s.
@@ -90,27 +103,30 @@ __device__ __forceinline__ uint32_t fp4_pack(const uint4& y, float r) {
   float2 f[Pack<T>::kElems / 2];
   pack_to_pairs<T>(y, f);
   const float2 r2 = make_float2(r, r);
-  uint32_t out = 0;
+  uint32_t b[Pack<T>::kElems / 2];
 #pragma unroll
   for (int i = 0; i < Pack<T>::kElems / 2; ++i) {
     // packed product: each half rounds like __fmul_rn, and only the
     // conversion consumes it
-    const uint32_t b = __nv_cvt_float2_to_fp4x2(__fmul2_rn(f[i], r2), __NV_E2M1, cudaRoundNearest);
-    out |= (b & 0xffu) << (8 * i);
+    b[i] = __nv_cvt_float2_to_fp4x2(__fmul2_rn(f[i], r2), __NV_E2M1, cudaRoundNearest);
   }
-  return out;
+  // byte i of the result is the low byte of b[i] (the bytes above the pack's
+  // Pack<T>::kElems / 2 are not stored)
+  const uint32_t low = __byte_perm(b[0], b[1], 0x0040);
+  if constexpr (Pack<T>::kElems / 2 == 4) {
+    return __byte_perm(low, __byte_perm(b[2], b[3], 0x0040), 0x5410);
+  } else {
+    return low;
+  }
 }
 
 template <typename T>
 __device__ __forceinline__ float pack_peak(const uint4& y) {
   if constexpr (sizeof(T) == 2) {
-    // |y| by clearing the sign bits and the largest by a packed max, both
-    // exact on the 16-bit values
+    // |y| and the largest by packed abs and max, both exact on the 16-bit
+    // values
     using V2 = std::conditional_t<std::is_same_v<T, __half>, __half2, __nv_bfloat162>;
-    auto magnitudes = [](uint32_t w) {
-      w &= 0x7fff7fffu;
-      return *reinterpret_cast<const V2*>(&w);
-    };
+    auto magnitudes = [](uint32_t w) { return __habs2(*reinterpret_cast<const V2*>(&w)); };
     const V2 m = __hmax2(__hmax2(magnitudes(y.x), magnitudes(y.y)),
                          __hmax2(magnitudes(y.z), magnitudes(y.w)));
     float lo, hi;
@@ -147,12 +163,14 @@ __device__ __forceinline__ void store_fp4(uint8_t* p, uint32_t v) {
   }
 }
 
-// Quantise one pack c of row `row` (y already normalised); every lane of the
-// warp calls this (the shuffles need them all), `valid` marks real packs.
-// `multipliers`: the per-code table, or nullptr to divide here.
+// Quantise one pack c of a row (y already normalised); every lane of the warp
+// calls this (the shuffles need them all), `valid` marks real packs.
+// `out_row`: the row's first output byte; `scale_row`: scale_row_offset of the
+// row. `multipliers`: the per-code table, or nullptr to divide here.
 template <typename T>
-__device__ __forceinline__ void quantise_fp4_pack(const Fp4Args<T>& a, int64_t row, int c,
-                                                  bool valid, const uint4& y, float g,
+__device__ __forceinline__ void quantise_fp4_pack(const Fp4Args<T>& a, uint8_t* out_row,
+                                                  int64_t scale_row, int c, bool valid,
+                                                  const uint4& y, float g,
                                                   const float* multipliers) {
   constexpr int E = Pack<T>::kElems;
   constexpr int kLanes = kBlockElems / E;
@@ -160,10 +178,9 @@ __device__ __forceinline__ void quantise_fp4_pack(const Fp4Args<T>& a, int64_t r
   if (!valid) return;
   const uint8_t code = block_scale(peak, g);
   const float r = multipliers != nullptr ? multipliers[code] : multiplier_of(code, g);
-  store_fp4<T>(a.output + row * (a.hidden / 2) + static_cast<int64_t>(c) * (E / 2),
-               fp4_pack<T>(y, r));
+  store_fp4<T>(out_row + static_cast<uint32_t>(c) * (E / 2), fp4_pack<T>(y, r));
   if (c % kLanes == 0) {
-    a.block_scales[scale_offset(row, c / kLanes, a.scale_columns, a.tiled)] = code;
+    a.block_scales[scale_row + scale_block_offset(c / kLanes, a.tiled)] = code;
   }
 }
 
@@ -225,6 +242,8 @@ __global__ void __launch_bounds__(kMaxThreads, kMinBlocks) norm_fp4_cta_kernel(F
     const float inv = inverse_rms(block_allreduce_sum(__fadd_rn(acc.x, acc.y), partial, parity),
                                   n, a.epsilon);
     parity ^= 1;
+    uint8_t* out_row = a.output + row * (a.hidden / 2);
+    const int64_t scale_row = scale_row_offset(row, a.scale_columns, a.tiled);
 #pragma unroll
     for (int i = 0; i < kPacksPerThread; ++i) {
       const int c = threadIdx.x + i * blockDim.x;
@@ -235,7 +254,7 @@ __global__ void __launch_bounds__(kMaxThreads, kMinBlocks) norm_fp4_cta_kernel(F
             s[i], kWeightsInRegisters ? w[i] : load16(a.weight + static_cast<int64_t>(c) * E),
             inv);
       }
-      quantise_fp4_pack<T>(a, row, c, valid, y, g, kTable ? multipliers : nullptr);
+      quantise_fp4_pack<T>(a, out_row, scale_row, c, valid, y, g, kTable ? multipliers : nullptr);
     }
   }
 }
@@ -273,6 +292,8 @@ __global__ void __launch_bounds__(1024) norm_fp4_wide_kernel(Fp4Args<T> a) {
     const float inv = inverse_rms(block_allreduce_sum(__fadd_rn(acc.x, acc.y), partial, parity),
                                   n, a.epsilon);
     parity ^= 1;
+    uint8_t* out_row = a.output + row * (a.hidden / 2);
+    const int64_t scale_row = scale_row_offset(row, a.scale_columns, a.tiled);
     for (int k = 0; k < rounds; ++k) {
       const int c = threadIdx.x + k * blockDim.x;
       const bool valid = c < packs;
@@ -281,7 +302,7 @@ __global__ void __launch_bounds__(1024) norm_fp4_wide_kernel(Fp4Args<T> a) {
         y = normalise_pack<T>(load16(source + base + static_cast<int64_t>(c) * E),
                               load16(a.weight + static_cast<int64_t>(c) * E), inv);
       }
-      quantise_fp4_pack<T>(a, row, c, valid, y, g, multipliers);
+      quantise_fp4_pack<T>(a, out_row, scale_row, c, valid, y, g, multipliers);
     }
   }
 }
