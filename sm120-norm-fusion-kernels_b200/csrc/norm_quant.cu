@@ -316,13 +316,16 @@ int run_quant(const QuantArgs<T>& a, cudaStream_t stream) {
   // and w in up to 128 registers without spilling.
   if (vectorisable && packs <= 4 * 512) {
     // Chosen from measurements on B200 (graphs of back-to-back calls on cold
-    // data): rows wider than 512 packs with many rows run best as persistent
-    // 256-thread blocks holding four packs per thread, reading the weight
-    // from L1 per row so that more blocks fit on an SM. With the residual
-    // add, three blocks per SM: 65536 x 8192 bf16 static 577 us (607 with the
-    // weight in registers at two blocks), dynamic 590 (667), fp16 static 577
-    // (615). Without it, four: static 306 us (402), dynamic 381 (488).
-    // Narrower or fewer rows keep two packs per thread.
+    // data): rows wider than 512 packs with many rows run best as a
+    // 256-thread block per row holding four packs per thread, reading the
+    // weight from L1 per row so that more blocks fit on an SM: three per SM
+    // with the residual add, five without. Against the persistent grid of the
+    // same blocks (three / four per SM), 65536 x 8192 bf16 with the add:
+    // static 539 us against 575, dynamic 571 against 588; without it: static
+    // 296 against 304, dynamic 342 against 380, fp16 static 285 against 316;
+    // 2048 to 16384 rows and 5120- to 8192-wide rows gain 1-14% likewise
+    // (the persistent grid with the weight in registers took 607 us with the
+    // add). Narrower or fewer rows keep two packs per thread.
     DeviceInfo dev;
     int rc = current_device_info(&dev);
     if (rc != SM120N_OK) return rc;
@@ -330,9 +333,9 @@ int run_quant(const QuantArgs<T>& a, cudaStream_t stream) {
     if (packs <= 256) return launch_quant_cta<T, kAdd, kDynamic, 1, 256>(a, packs, stream);
     if (many_rows && packs > 512 && packs <= 1024) {
       if constexpr (kAdd) {
-        return launch_quant_cta<T, kAdd, kDynamic, 4, 256, 3, false>(a, packs, stream);
+        return launch_quant_cta<T, kAdd, kDynamic, 4, 256, 3, false>(a, packs, stream, true);
       } else {
-        return launch_quant_cta<T, kAdd, kDynamic, 4, 256, 4, false>(a, packs, stream);
+        return launch_quant_cta<T, kAdd, kDynamic, 4, 256, 5, false>(a, packs, stream, true);
       }
     }
     if (packs <= 1024) return launch_quant_cta<T, kAdd, kDynamic, 2, 512>(a, packs, stream);

@@ -594,13 +594,14 @@ int run_rows(const RowArgs<T>& a, Family family, cudaStream_t stream) {
         // Measured on one B200, graphs of back-to-back calls on cold data,
         // against the weight in registers: with the residual add at three
         // blocks per SM, 65536 x 8192 bf16 620 us (663), fp16 619 (661),
-        // 16384 x 8192 bf16 163 (172); without it at four, 65536 x 8192 bf16
-        // 326 us (479), 65536 x 4096 bf16 161 (193).
+        // 16384 x 8192 bf16 163 (172; four blocks per SM: no gain); without it
+        // at five, 65536 x 8192 bf16 314 us (479; four blocks per SM 329),
+        // 16384 x 8192 86 (four: 90.5), 32768 x 5120 105 (four: 106.5).
         if constexpr (kAdd) {
           return launch_cta<T, kAdd, 4, 256, 3, false>(a, round_up_warps((packs + 3) / 4), stream,
                                                        true);
         } else {
-          return launch_cta<T, kAdd, 4, 256, 4, false>(a, round_up_warps((packs + 3) / 4), stream,
+          return launch_cta<T, kAdd, 4, 256, 5, false>(a, round_up_warps((packs + 3) / 4), stream,
                                                        true);
         }
       }
