@@ -21,10 +21,10 @@
 // 16-byte packs) and a vectorised two-pass kernel for wider rows. A 16-element
 // block spans 2 packs of a 16-bit type (4 of fp32) held by adjacent lanes, so
 // its maximum takes one (two) shuffles and no extra barrier. r takes one of
-// 256 values (one per e4m3 code): blocks that process many rows divide once
-// per code into a shared-memory table, so their per-block work has no
-// division; blocks with a row or two divide per block instead (filling the
-// table would cost more than it saves).
+// 256 values (one per e4m3 code): the 256-thread many-row launch (a block
+// per row) and the two-pass kernel divide once per code into a shared-memory
+// table, one division per thread, so their per-block work has no division;
+// the other launch shapes divide per 16-element block.
 #include <cuda_fp4.h>
 #include <cuda_fp8.h>
 
@@ -322,13 +322,18 @@ int fp4_grid(Kernel kernel, int threads, int64_t rows, int* grid) {
 
 template <typename T, bool kAdd, int kPPT, int kMaxThreads, int kMinBlocks = 1,
           bool kTable = false, bool kWeightsInRegisters = true>
-int launch_fp4_cta(const Fp4Args<T>& a, int packs, cudaStream_t stream) {
+int launch_fp4_cta(const Fp4Args<T>& a, int packs, cudaStream_t stream,
+                   bool one_row_per_block = false) {
   auto kernel =
       norm_fp4_cta_kernel<T, kAdd, kPPT, kMaxThreads, kMinBlocks, kTable, kWeightsInRegisters>;
   const int threads = (((packs + kPPT - 1) / kPPT) + kWarpSize - 1) / kWarpSize * kWarpSize;
   int grid = 0;
-  int rc = fp4_grid(kernel, threads, a.rows, &grid);
-  if (rc != SM120N_OK) return rc;
+  if (one_row_per_block && a.rows <= INT32_MAX) {
+    grid = static_cast<int>(a.rows);
+  } else {
+    int rc = fp4_grid(kernel, threads, a.rows, &grid);
+    if (rc != SM120N_OK) return rc;
+  }
   return launch(kernel, dim3(grid), dim3(threads), 0, stream, a);
 }
 
@@ -343,10 +348,15 @@ int run_fp4(const Fp4Args<T>& a, cudaStream_t stream) {
   const bool many_rows = a.rows >= 8 * static_cast<int64_t>(dev.sm_count);
   if (packs <= 256) return launch_fp4_cta<T, kAdd, 1, 256>(a, packs, stream);
   if (many_rows && packs > 512 && packs <= 1024) {
-    // weights read from L1 per row: 61 registers and four blocks per SM
-    // instead of 80 and three (bf16 65536 x 8192: 588 us against 643,
-    // 16384 x 8192: 158 against 171; bit-identical results)
-    return launch_fp4_cta<T, kAdd, 4, 256, 4, true, false>(a, packs, stream);
+    // A 256-thread block per row, the weight read from L1 per row: 60
+    // registers and four blocks per SM instead of 80 and three (persistent
+    // grids, bf16 65536 x 8192: 588 us against 643), then a block per row
+    // instead of the persistent grid (65536 x 8192 with the add 538.5 us
+    // against 568, fp16 32768 x 5120 183.5 against 198, 16384 x 8192 146
+    // against 150; without the add 427 against 425). A block fills the
+    // 256-entry multiplier table with one division per thread, no more than
+    // dividing per 16-element block would cost. Bit-identical results.
+    return launch_fp4_cta<T, kAdd, 4, 256, 4, true, false>(a, packs, stream, true);
   }
   if (packs <= 1024) return launch_fp4_cta<T, kAdd, 2, 512, 2>(a, packs, stream);
   if (packs <= 2048) return launch_fp4_cta<T, kAdd, 4, 512>(a, packs, stream);
