@@ -362,6 +362,30 @@ def test_norm_quant_many_wide_rows_exact(dtype, add, dynamic):
         assert_bitwise_equal(r_out, want_r, what="residual")
 
 
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
+@pytest.mark.parametrize("rows,hidden", [(500, 4096), (600, 4096), (1150, 4096), (1150, 3072),
+                                         (1150, 2048)])
+@pytest.mark.parametrize("add", [False, True])
+@pytest.mark.parametrize("dynamic", [False, True])
+def test_norm_quant_mid_rows_exact(dtype, rows, hidden, add, dynamic):
+    """Two-pack calls on either side of the point where the blocks holding the
+    weight in registers stop covering every row at once (dynamic scales then
+    read the weight from L1 at more blocks per SM)."""
+    g = gen(rows + hidden + add + 2 * dynamic)
+    limit = 8 if add else 16
+    x = exact_values((rows, hidden), dtype, g, limit)
+    r = exact_values((rows, hidden), dtype, g, limit) if add else None
+    w = weights(hidden, dtype, g)
+    scale = None if dynamic else torch.tensor([0.03])
+    q, scales, r_out = run_quant(x, w, r, scale)
+    want_q, want_scales, want_r = ex.rms_norm_fp8_quant(x, w, residual=r, scale=scale)
+    assert torch.equal(q.view(torch.uint8), want_q.view(torch.uint8))
+    if dynamic:
+        assert_bitwise_equal(scales, want_scales.reshape(-1), what="token scales")
+    if add:
+        assert_bitwise_equal(r_out, want_r, what="residual")
+
+
 @pytest.mark.parametrize("dtype", DTYPES)
 @pytest.mark.parametrize("hidden", [1024, 4096, 32768])
 @pytest.mark.parametrize("dynamic", [False, True])
