@@ -18,8 +18,9 @@
 //          1, 2 or 4 packs per thread; one barrier per row (double-buffered
 //          partial sums). The default for every row up to 16 KiB.
 //   staged a block per row, the row and the weight brought into shared memory
-//          by the TMA engine (cp.async.bulk, mbarrier completion); 4-16 KiB
-//          rows in calls of 16-128 MiB.
+//          by the TMA engine (cp.async.bulk, mbarrier completion); with the
+//          residual add 4-16 KiB rows in calls of 16-128 MiB, without it
+//          8-16 KiB rows in calls of 16-32 MiB.
 //   bulk   persistent blocks, rows staged through shared memory by the TMA
 //          engine (cp.async.bulk, mbarrier completion); rows of 16-32 KiB.
 //   wide   one thread block per row, any 16-byte-aligned row; two passes
@@ -554,14 +555,19 @@ int run_rows(const RowArgs<T>& a, Family family, cudaStream_t stream) {
     if (rc != SM120N_OK) return rc;
     many_rows = a.rows >= 8 * static_cast<int64_t>(dev.sm_count);
     const int64_t input_bytes = a.rows * static_cast<int64_t>(a.hidden) * sizeof(T);
-    if (packs >= 256 && packs <= 1024 && input_bytes >= (int64_t{16} << 20) &&
-        input_bytes <= (int64_t{128} << 20)) {
-      // 4-16 KiB rows, 16-128 MiB of input: rows staged in shared memory, a
-      // block per row (bf16 2048 x 4096: 13.6-13.8 us against 15.0-15.1;
-      // 4096 x 4096: 26.8-27.7 against 28.7; 1024 x 8192: 13.7-14.0 against
-      // 14.5-14.9; 4096 x 2048: 13.7 against 14.2-14.4). Below 16 MiB the
-      // register kernels win (1024 x 4096: 7.3 against 7.1 us); far above,
-      // the four-pack kernel matches it (16384 x 8192: 162 us both).
+    // Rows staged in shared memory, a block per row: with the residual add,
+    // 4-16 KiB rows in calls of 16-128 MiB of input (bf16 2048 x 4096: 13.3
+    // us against 13.8; 4096 x 4096: 24.6 against 25.6; 1024 x 8192: 13.3
+    // against 14.4; 16384 x 2048: 47.0 against 50.7); without it only 8-16
+    // KiB rows in calls of 16-32 MiB (1024 x 8192: 9.3 against 10.0; from
+    // 32 MiB up the five-block register kernel wins: 4096 x 8192 28.7 us
+    // against 32.8, 4096 x 4096 15.4 against 16.4; 4096 x 2048 8.0 against
+    // 8.7). Below 16 MiB the register kernels win (1024 x 4096: 7.1 against
+    // 7.3 us); far above, the four-pack kernel matches it (16384 x 8192: 162
+    // us both).
+    const bool staged = kAdd ? packs >= 256 && input_bytes <= (int64_t{128} << 20)
+                             : packs >= 512 && input_bytes < (int64_t{32} << 20);
+    if (staged && packs <= 1024 && input_bytes >= (int64_t{16} << 20)) {
       family = Family::kStaged;
     } else if (packs <= 256) {
       family = a.rows >= 1024 ? Family::kCta : Family::kCtaOnePack;

@@ -255,9 +255,12 @@ def test_staged_rows_match_the_oracle_and_version_2(rows, hidden, dtype):
     check_norm(x[sample].cpu(), expected, what="output (sampled rows)")
     assert_bitwise_equal(r, r2, what="residual vs version 2")
     assert_bitwise_equal(x, x2, what="output vs version 2")
-    # plain RMSNorm at the same size: oracle on the sample, version 1 bit for bit
+    # plain RMSNorm at the same size: oracle on the sample; where auto dispatch
+    # stages it too (8-16 KiB rows, 16-32 MiB calls), version 1 bit for bit
     y = rms_norm(r, w)
-    assert_bitwise_equal(y, rms_norm(r, w, version=1), what="rms_norm vs version 1")
+    row_bytes = hidden * r.element_size()
+    if row_bytes >= 8192 and rows * row_bytes < (32 << 20):
+        assert_bitwise_equal(y, rms_norm(r, w, version=1), what="rms_norm vs version 1")
     check_norm(y[sample].cpu(), expect_rms_norm(r[sample], w), what="rms_norm (sampled rows)")
 
 
