@@ -168,6 +168,28 @@ def test_reference_exports_match_the_oracle_on_cpu():
     assert_ulp_close(c, a)
 
 
+def test_fp32_norm_bar_grows_with_the_row_length():
+    """The fp32 norm bar: 4 ulp up to 1024 elements, 4 * ceil(sqrt(n / 1024))
+    beyond; 16-bit outputs keep 1 ulp at every length."""
+    from numerics import default_norm_ulps
+    assert [default_norm_ulps(torch.float32, n) for n in (1, 1024, 1025, 2560, 4096, 8192)] == \
+        [4, 4, 8, 8, 8, 12]
+    assert default_norm_ulps(torch.bfloat16, 8192) == 1 and default_norm_ulps(torch.float16, 8192) == 1
+
+
+@pytest.mark.parametrize("hidden", [1024, 2560, 8192])
+def test_fp32_bar_covers_two_summation_orders(hidden):
+    """Two CPU restatements that add the squares in different fp32 orders (the
+    C oracle's lane tree and PyTorch's reduction) stay within the bar."""
+    from oracle import oracle
+    from numerics import assert_ulp_close
+    oracle.build()
+    g = torch.Generator().manual_seed(hidden)
+    x = torch.randn(64, hidden, generator=g)
+    w = 1 + 0.1 * torch.randn(hidden, generator=g)
+    assert_ulp_close(oracle.rms_norm(x, w), sm120_rmsnorm.rms_norm_reference(x, w), what="fp32 rms_norm")
+
+
 def test_wait_limit_setting_clamps_and_restores():
     default = capi.wait_limit()
     assert default == 1 << 22
