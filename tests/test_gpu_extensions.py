@@ -345,8 +345,8 @@ def test_norm_quant_exact(dtype, hidden, add, dynamic):
 @pytest.mark.parametrize("add", [False, True])
 @pytest.mark.parametrize("dynamic", [False, True])
 def test_norm_quant_many_wide_rows_exact(dtype, add, dynamic):
-    """1200 rows of 8192: more than eight rows per SM, the persistent
-    four-packs-per-thread launch."""
+    """1200 rows of 8192: more than eight rows per SM, the many-row launch (a
+    256-thread block per row, four packs per thread)."""
     g = gen(8192 + add + 2 * dynamic)
     limit = 8 if add else 16
     x = exact_values((1200, 8192), dtype, g, limit)
@@ -476,18 +476,22 @@ def test_nvfp4_exact(dtype, hidden, add, tiled):
 
 
 @pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
-def test_nvfp4_many_wide_rows_exact(dtype):
-    """1200 rows of 8192 (the persistent four-packs-per-thread launch), tiled
-    scales over a row count that is not a multiple of 128."""
-    g = gen(1200)
-    x = exact_values((1200, 8192), dtype, g, 8)
-    r = exact_values((1200, 8192), dtype, g, 8)
+@pytest.mark.parametrize("add", [False, True])
+def test_nvfp4_many_wide_rows_exact(dtype, add):
+    """1200 rows of 8192 (the many-row launch: a 256-thread block per row, four
+    packs per thread), tiled scales over a row count that is not a multiple of
+    128."""
+    g = gen(1200 + add)
+    limit = 8 if add else 16
+    x = exact_values((1200, 8192), dtype, g, limit)
+    r = exact_values((1200, 8192), dtype, g, limit) if add else None
     w = weights(8192, dtype, g)
     q, scales, r_out = run_fp4(x, w, 500.0, r, True)
     want_q, want_scales, want_r = ex.rms_norm_nvfp4_quant(x, w, 500.0, residual=r, tiled=True)
     assert torch.equal(scales, want_scales)
     assert torch.equal(q, want_q)
-    assert_bitwise_equal(r_out, want_r, what="residual")
+    if add:
+        assert_bitwise_equal(r_out, want_r, what="residual")
 
 
 @pytest.mark.parametrize("dtype", DTYPES)

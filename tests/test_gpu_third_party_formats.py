@@ -122,7 +122,7 @@ def _e2m1_steps(a, b):
 
 @needs_vllm
 @pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
-@pytest.mark.parametrize("rows,hidden", [(256, 4096), (200, 8192)])
+@pytest.mark.parametrize("rows,hidden", [(256, 4096), (200, 8192), (1200, 8192)])
 @pytest.mark.parametrize("add", [False, True])
 def test_nvfp4_codes_and_tiled_scales_match_vllm_exact_inputs(dtype, rows, hidden, add):
     g = torch.Generator(device=DEV).manual_seed(rows + hidden + add)
