@@ -655,7 +655,17 @@ class PerConfig:
             return [lambda i=i, x=x, r=r: keep.__setitem__(i, fn(x, r, w))
                     for i, (x, r) in enumerate(sets)]
 
+        def sm_copy():
+            # a plain elementwise kernel on the SMs that reads and writes the
+            # same bytes (d = s * 1): the protocol's own floor for a call of
+            # this size (a same-dtype copy_ in a graph runs on the copy engines)
+            pairs = [(torch.randn(2 * t * h, device="cuda", generator=g).to(torch.bfloat16),
+                      torch.empty(2 * t * h, device="cuda", dtype=torch.bfloat16))
+                     for _ in range(len(sets))]
+            return [lambda s=s, d=d: torch.mul(s, 1, out=d) for s, d in pairs]
+
         cmp = self.comparators({
+            "sm_copy_same_bytes": sm_copy,
             "reference_kernels": self.ref and (lambda: [
                 lambda x=x, r=r: self.ref.fused_add_rms_norm_inplace(x, r, w) for x, r in sets]),
             "torch_native": lambda: kept(torch_native_fused),
