@@ -315,6 +315,18 @@ def sets_for(nbytes: int) -> int:
     return max(1, min(64, (256 << 20) // max(nbytes, 1)))
 
 
+def sm_copy_calls(nbytes: int, g: torch.Generator) -> list:
+    """Calls of a plain elementwise kernel on the SMs (d = s * 1, bf16) that
+    reads nbytes / 2 and writes nbytes / 2, on distinct buffer sets: the
+    protocol's own floor for a call that moves nbytes (a same-dtype copy_ in a
+    graph runs on the copy engines instead)."""
+    n = max(1, nbytes // 4)
+    pairs = [(torch.randn(n, device="cuda", generator=g).to(torch.bfloat16),
+              torch.empty(n, device="cuda", dtype=torch.bfloat16))
+             for _ in range(sets_for(nbytes))]
+    return [lambda s=s, d=d: torch.mul(s, 1, out=d) for s, d in pairs]
+
+
 def rope_table(n: int, rotary: int = 128, device="cuda", dtype=torch.float32):
     inv = 1.0 / (1e6 ** (torch.arange(0, rotary, 2, dtype=torch.float32, device=device) / rotary))
     f = torch.outer(torch.arange(n, dtype=torch.float32, device=device), inv)
@@ -655,17 +667,8 @@ class PerConfig:
             return [lambda i=i, x=x, r=r: keep.__setitem__(i, fn(x, r, w))
                     for i, (x, r) in enumerate(sets)]
 
-        def sm_copy():
-            # a plain elementwise kernel on the SMs that reads and writes the
-            # same bytes (d = s * 1): the protocol's own floor for a call of
-            # this size (a same-dtype copy_ in a graph runs on the copy engines)
-            pairs = [(torch.randn(2 * t * h, device="cuda", generator=g).to(torch.bfloat16),
-                      torch.empty(2 * t * h, device="cuda", dtype=torch.bfloat16))
-                     for _ in range(len(sets))]
-            return [lambda s=s, d=d: torch.mul(s, 1, out=d) for s, d in pairs]
-
         cmp = self.comparators({
-            "sm_copy_same_bytes": sm_copy,
+            "sm_copy_same_bytes": lambda: sm_copy_calls(nbytes, g),
             "reference_kernels": self.ref and (lambda: [
                 lambda x=x, r=r: self.ref.fused_add_rms_norm_inplace(x, r, w) for x, r in sets]),
             "torch_native": lambda: kept(torch_native_fused),
@@ -719,10 +722,11 @@ class PerConfig:
         del calls
         torch.cuda.empty_cache()
         t1 = self.whole_on_rank0(lambda s, e: build(s, e)) if sharded else None
-        cmp = self.comparators({"reference_kernels": self.ref and (
-            lambda: build(0, b_total, self.ref))})
-        torch.cuda.empty_cache()
         nbytes = qk_kv_bytes(b_total, hq, hk, 2)
+        cmp = self.comparators({
+            "sm_copy_same_bytes": lambda: sm_copy_calls(nbytes, self.g),
+            "reference_kernels": self.ref and (lambda: build(0, b_total, self.ref))})
+        torch.cuda.empty_cache()
         return self.put(name, us, nbytes, sharded=sharded, t1=t1, cmp=cmp)
 
     def qk_no_kv(self):
