@@ -1523,6 +1523,82 @@ def pytorch_cpu_reference(threads: int, rows: int = 2048, calls: int = 5) -> dic
             "sample": f"{calls} calls on {rows} of the 65536 rows, {elapsed:.2f} s"}
 
 
+def pytorch_cpu_per_config(threads: int) -> dict:
+    """The reference's PyTorch math (restated op for op in
+    sm120_rmsnorm/reference.py) on the host CPU for the small configurations,
+    as the reference's own CPU baseline measures them: per call, after a
+    warm-up call, at least 200 calls or 20 ms (time.perf_counter), all host
+    threads; keyed like the GPU arm's per-config entries, with GB/s from the
+    same byte formulas. The Q/K-KV decode includes the two paged-cache stores."""
+    import importlib.util
+
+    path = ROOT / "sm120-norm-fusion-kernels_b200" / "sm120_rmsnorm" / "reference.py"
+    spec = importlib.util.spec_from_file_location("config_reference_math", path)
+    ref = importlib.util.module_from_spec(spec)
+    spec.loader.exec_module(ref)
+    torch.set_num_threads(threads)
+    g = torch.Generator().manual_seed(97)
+
+    def per_call_us(fn):
+        fn()
+        calls, t0 = 0, time.perf_counter()
+        while calls < 200 or time.perf_counter() - t0 < 0.02:
+            fn()
+            calls += 1
+            if calls >= 200 and time.perf_counter() - t0 >= 0.02:
+                break
+        return (time.perf_counter() - t0) / calls * 1e6
+
+    out = {}
+
+    def put(name, us, nbytes):
+        out[name] = {"us": round(us, 2), "gbs": round(nbytes / (us * 1e-6) / 1e9, 3)}
+
+    for t in (1, 4, 16, 64, 256):
+        x = torch.randn(t, 1024, generator=g)
+        w = 1 + 0.1 * torch.randn(1024, generator=g)
+        put(f"rms_norm fp32 {t}x1024", per_call_us(lambda: ref.rms_norm_reference(x, w, EPS)),
+            rms_bytes(t, 1024, 4))
+    step_us, step_bytes = 0.0, 0
+    for t, h, name in sweep_shapes():
+        dt = DTYPES[name]
+        x = torch.randn(t, h, generator=g).to(dt)
+        r = torch.randn(t, h, generator=g).to(dt)
+        w = (1 + 0.1 * torch.randn(h, generator=g)).to(dt)
+        us = per_call_us(lambda: ref.fused_add_rms_norm_reference(x, r, w, EPS))
+        step_us += us
+        step_bytes += fused_bytes(t, h, 2)
+        if (t, h, name) == (1024, 4096, "bf16"):
+            put("fused_add bf16 1024x4096 (dominant sweep call)", us, fused_bytes(t, h, 2))
+    put("fused_add sweep 48 calls (step)", step_us, step_bytes)
+    cache = rope_table(32768, device="cpu")
+    bf = torch.bfloat16
+    qw = (1 + 0.1 * torch.randn(128, generator=g)).to(bf)
+    kw = (1 + 0.1 * torch.randn(128, generator=g)).to(bf)
+    q = torch.randn(1, 16, 128, generator=g).to(bf)
+    k = torch.randn(1, 8, 128, generator=g).to(bf)
+    v = torch.randn(1, 8, 128, generator=g).to(bf)
+    pos = torch.randint(0, 32768, (1,), generator=g)
+    slots = torch.randint(0, 2048 * 16, (1,), generator=g)
+    kc = torch.zeros(2048 * 16, 8, 128, dtype=bf)
+    vc = torch.zeros_like(kc)
+
+    def qk_kv():
+        qo, ko = ref.qk_rms_norm_rope_reference(q, k, qw, kw, pos, cache, EPS)
+        kc[slots] = ko
+        vc[slots] = v
+
+    put("qk_kv decode bf16 B=1 16/8", per_call_us(qk_kv), qk_kv_bytes(1, 16, 8, 2))
+    for t in (1, 4, 16, 64, 256):
+        qt = torch.randn(t, 16, 128, generator=g).to(bf)
+        kt = torch.randn(t, 8, 128, generator=g).to(bf)
+        pt = torch.arange(t)
+        put(f"qk (no kv) bf16 T={t} 16/8",
+            per_call_us(lambda: ref.qk_rms_norm_rope_reference(qt, kt, qw, kw, pt, cache, EPS)),
+            qk_bytes(t, 16, 8, 2))
+    return out
+
+
 def reference_arm(args) -> dict:
     """The reference path's CPU implementation (C restatement of its PyTorch
     oracle) on the host cores, on the headline workload, in REPEAT_PROCESSES
@@ -1554,6 +1630,7 @@ def reference_arm(args) -> dict:
                 "which cannot travel; this is its C restatement (oracle/norm_oracle.c), pinned "
                 "to the reference's own outputs by the golden-vector tests",
         "reference_pytorch_cpu": pytorch_cpu_reference(threads),
+        "reference_pytorch_cpu_per_config": pytorch_cpu_per_config(threads),
         "reference_kernels_b200": reference_kernels_gpu(args),
     }
 

@@ -75,3 +75,15 @@ def test_byte_models(bench):
     assert bench.fused_bytes(1024, 4096, 2) == 33_562_624
     assert bench.qk_kv_bytes(1024, 32, 8, 2) == 27_800_064
     assert bench.qk_bytes(1, 16, 8, 2) == 1 * (2 * 128 * 48 + 8 + 512) + 512
+
+
+def test_pytorch_cpu_per_config_names_match_the_gpu_arm(bench):
+    """The reference arm's per-configuration CPU timings use the GPU arm's
+    per-config names, so the two lines can be read side by side."""
+    r = bench.pytorch_cpu_per_config(2)
+    expected = {f"rms_norm fp32 {t}x1024" for t in (1, 4, 16, 64, 256)} | \
+        {f"qk (no kv) bf16 T={t} 16/8" for t in (1, 4, 16, 64, 256)} | \
+        {"fused_add sweep 48 calls (step)", "fused_add bf16 1024x4096 (dominant sweep call)",
+         "qk_kv decode bf16 B=1 16/8"}
+    assert set(r) == expected
+    assert all(v["us"] > 0 and v["gbs"] > 0 for v in r.values())
