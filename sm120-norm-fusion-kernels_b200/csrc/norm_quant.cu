@@ -319,7 +319,7 @@ int run_quant(const QuantArgs<T>& a, cudaStream_t stream) {
     // data): rows wider than 512 packs with many rows run best as a
     // 256-thread block per row holding four packs per thread, reading the
     // weight from L1 per row so that more blocks fit on an SM: three per SM
-    // with the residual add, five without. Against the persistent grid of the
+    // with the residual add (four with dynamic scales), five without. Against the persistent grid of the
     // same blocks (three / four per SM), 65536 x 8192 bf16 with the add:
     // static 539 us against 575, dynamic 571 against 588; without it: static
     // 296 against 304, dynamic 342 against 380, fp16 static 285 against 316;
@@ -332,7 +332,11 @@ int run_quant(const QuantArgs<T>& a, cudaStream_t stream) {
     const bool many_rows = a.rows >= 8 * static_cast<int64_t>(dev.sm_count);
     if (packs <= 256) return launch_quant_cta<T, kAdd, kDynamic, 1, 256>(a, packs, stream);
     if (many_rows && packs > 512 && packs <= 1024) {
-      if constexpr (kAdd) {
+      if constexpr (kAdd && kDynamic) {
+        // the row maximum's second barrier per row wants a fourth block per
+        // SM (65536 x 8192 bf16 541 us against 571 at three)
+        return launch_quant_cta<T, kAdd, kDynamic, 4, 256, 4, false>(a, packs, stream, true);
+      } else if constexpr (kAdd) {
         return launch_quant_cta<T, kAdd, kDynamic, 4, 256, 3, false>(a, packs, stream, true);
       } else {
         return launch_quant_cta<T, kAdd, kDynamic, 4, 256, 5, false>(a, packs, stream, true);
